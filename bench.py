@@ -1,0 +1,389 @@
+"""Benchmark: exact top-k search QPS on B200, with roofline and CPU baseline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+One step = one search of a query batch against the corpus, with queries and
+corpus already resident in HBM (`value`); `e2e` repeats it through the public
+API from pinned host queries (fp32) to host results. Default workload (config
+c2): 1M x 768 fp16 unit-norm corpus PER GPU, batch 256, k=10, cosine. With N>1
+ranks (torchrun) the corpus is row-sharded: rank r holds its own 1M rows, each
+step is a full sharded search (local fused top-k + NCCL all-gather + merge), and
+`value` counts query x 1M-row-shard units per second over all ranks (N*b/t).
+
+--impl reference times the reference's CPU path restated in numpy (oracle/,
+fp32 matmul + top-k with the reference's chunked merge) on the host cores, on a
+bounded sample of the same workload, scaled to the same unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "cuda-vector-search_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "QPS and % roofline (TC TFLOP/s or HBM GB/s), 1M×768 b256 k10, 1–8 B200"
+CHUNK = 1 << 18
+
+CONFIGS = {
+    # name: rows per GPU, dim, batch, k, metric
+    "c1": dict(n=100_000, d=384, b=32, k=10, metric="cosine"),
+    "c2": dict(n=1_000_000, d=768, b=256, k=10, metric="cosine"),
+    "c3": dict(n=4_000_000, d=768, b=1, k=10, metric="ip"),
+    "c4k100": dict(n=1_000_000, d=384, b=256, k=100, metric="cosine"),
+    "c4k256": dict(n=1_000_000, d=384, b=256, k=256, metric="cosine"),
+    "c5": dict(n=16_000_000, d=768, b=1024, k=100, metric="cosine"),
+}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic(config: str):
+    """Per-launch DRAM bytes of the search kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    j = json.loads(p.read_text())
+    return j.get(config)
+
+
+def workload_name(cfg) -> str:
+    return (f"{cfg['n'] // 1000}k x {cfg['d']} fp16 unit-norm corpus per GPU, batch {cfg['b']}, "
+            f"k={cfg['k']}, {cfg['metric']}")
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's fp32 CPU path restated in numpy (oracle/)
+# ---------------------------------------------------------------------------
+def cpu_sample(cfg, rows: int, seed: int):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, cfg["d"]), dtype=np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    q = rng.standard_normal((cfg["b"], cfg["d"]), dtype=np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    return x.astype(np.float16), q.astype(np.float16)
+
+
+def time_cpu_step(cfg, x16, q16):
+    """One bounded step of the CPU path; returns seconds."""
+    import numpy as np
+
+    from oracle import exact_topk, normalize_rows_fp16
+
+    t0 = time.perf_counter()
+    q = normalize_rows_fp16(q16) if cfg["metric"] == "cosine" else q16
+    exact_topk(q.astype(np.float32), x16, cfg["k"])
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(cfg, budget_s: float = 12.0):
+    import numpy as np  # noqa: F401
+
+    rows = min(cfg["n"], 131072)
+    x16, q16 = cpu_sample(cfg, rows, seed=7)
+    time_cpu_step(cfg, x16[:4096], q16)  # warm the BLAS threads
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < 3 or (time.perf_counter() - t_start < budget_s and len(times) < 20):
+        times.append(time_cpu_step(cfg, x16, q16))
+    t = statistics.median(times)
+    qps = cfg["b"] / (t * cfg["n"] / rows)
+    return {
+        "value": round(qps, 2),
+        "unit": "QPS",
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": (f"all {cfg['b']} queries x {rows} of {cfg['n']} corpus rows per step "
+                   f"(median of {len(times)}), scaled linearly to {cfg['n']} rows; numpy fp32 matmul + "
+                   f"top-k with the reference's chunked merge (oracle/exact.py)"),
+    }
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    W = max(args.warmup, 0)
+    rows = min(cfg["n"], 65536)
+    x16, q16 = cpu_sample(cfg, rows, seed=7)
+    for _ in range(min(W, 2)):
+        time_cpu_step(cfg, x16, q16)
+    times = [time_cpu_step(cfg, x16, q16) for _ in range(args.steps)]
+    t = sum(times) / len(times) * cfg["n"] / rows
+    qps = cfg["b"] / t
+    base = {
+        "value": round(qps, 2),
+        "unit": "QPS",
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": (f"each step: all {cfg['b']} queries x {rows} of {cfg['n']} corpus rows, scaled "
+                   f"linearly to {cfg['n']} rows; numpy restatement of the reference CPU path (oracle/)"),
+    }
+    out = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(qps, 2),
+        "unit": "QPS",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": W,
+        "ms_per_step": round(t * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": workload_name(cfg), **cfg},
+        "cpu_baseline": base,
+        "e2e": {"value": round(qps, 2), "unit": "QPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def make_shard(torch, n, d, seed, first_chunk, device):
+    """Unit-norm fp16 rows generated per 2^18-row chunk with a per-GLOBAL-chunk
+    seed (reference bench/bench_gpu.py:36-43), so any sharding yields the same
+    global corpus."""
+    x = torch.empty((n, d), dtype=torch.float16, device=device)
+    for c, start in enumerate(range(0, n, CHUNK)):
+        g = torch.Generator(device=device).manual_seed(seed * 100003 + first_chunk + c)
+        blk = torch.randn(min(CHUNK, n - start), d, device=device, generator=g)
+        x[start : start + blk.shape[0]] = (blk / blk.norm(dim=1, keepdim=True)).half()
+    return x
+
+
+def make_queries(torch, b, d, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(b, d, device=device, generator=g)
+    return (q / q.norm(dim=1, keepdim=True)).half()
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:  # nvidia-smi missing: report no clocks
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in rows for j in range(4) if r[5 + j].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import cuda_vector_search as cvs
+    from cuda_vector_search import _ext
+
+    mod = _ext.load()
+    n, d, b, k = cfg["n"], cfg["d"], cfg["b"], cfg["k"]
+    chunks_per_shard = (n + CHUNK - 1) // CHUNK
+    x = make_shard(torch, n, d, seed=1, first_chunk=rank * chunks_per_shard, device=dev)
+    if world > 1:
+        index = cvs.ShardedIndex(x, metric=cfg["metric"], device=dev, copy=False)
+        local_index = index.local
+    else:
+        index = cvs.Index(x, metric=cfg["metric"], device=dev, copy=False)
+        local_index = index
+    q_dev = make_queries(torch, b, d, seed=2, device=dev)
+    q_host = q_dev.float().cpu().pin_memory()
+    del x
+
+    def step(q):
+        return index.search(q, k)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step(q_dev)
+    barrier()
+
+    # Timed region: device-resident queries, CUDA events on the launching stream.
+    stream = torch.cuda.current_stream()
+    ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, bb in ev_pairs:  # torch creates the CUDA event on first record
+        a.record(stream)
+        bb.record(stream)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    t0.record(stream)
+    for s in range(args.steps):
+        mod.set_profile_events(ev_pairs[s][0].cuda_event, ev_pairs[s][1].cuda_event)
+        step(q_dev)
+    t1.record(stream)
+    barrier()
+    mod.set_profile_events(0, 0)
+    ms_total = t0.elapsed_time(t1)
+    kern_ms = [a.elapsed_time(bb) for a, bb in ev_pairs]
+
+    # End to end through the public API: pinned host fp32 queries in, host results out.
+    e2e_t0, e2e_t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e2e_t0.record(stream)
+    for _ in range(args.steps):
+        v, i = index.search(q_host, k)
+        v_host, i_host = v.cpu(), i.cpu()
+    e2e_t1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    e2e_ms_total = e2e_t0.elapsed_time(e2e_t1)
+
+    tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_total, e2e_ms_total, kern_total = tt.tolist()
+    ms = ms_total / args.steps
+    kern_avg = kern_total / args.steps
+    value = world * b / (ms / 1e3)
+    e2e_value = world * b / (e2e_ms_total / args.steps / 1e3)
+
+    if rank == 0:
+        hbm_peak, tc_peak, peak_src = load_peaks()
+        d_pad = local_index._x.shape[1]
+        flops = 2.0 * b * n * d
+        alg_bytes = 2.0 * n * d_pad + 2.0 * b * d_pad + 12.0 * b * k
+        tflops = flops / (kern_avg / 1e3) / 1e12
+        gbs = alg_bytes / (kern_avg / 1e3) / 1e9
+        tc_time = flops / (tc_peak * 1e12)
+        hbm_time = alg_bytes / (hbm_peak * 1e9)
+        bound = "tensor" if tc_time >= hbm_time else "hbm"
+        traffic = load_traffic(args.config)
+        roof_tc = {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                   "frac": round(tflops / tc_peak, 4), "traffic": traffic,
+                   "note": f"bf16 dense burst peak, {peak_src}"}
+        roof_hbm = {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(gbs / hbm_peak, 4), "traffic": traffic,
+                    "note": f"copy bandwidth, {peak_src}; algorithmic bytes = corpus + queries + results"}
+        roofline = roof_tc if bound == "tensor" else roof_hbm
+        launches_per_step = 3 if world == 1 else 4  # ingest, search, merge (+ shard merge)
+        out = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "QPS",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic",
+            "config": {
+                "workload": workload_name(cfg),
+                "config": args.config,
+                "rows_per_gpu": n, "total_rows": n * world, "dim": d, "batch": b, "k": k,
+                "metric": cfg["metric"],
+                "l2": f"inputs larger than L2 ({2 * n * d_pad / 1e9:.2f} GB corpus per GPU vs 126 MB L2)",
+                "value_unit": "queries x 1M-row shards per second over all ranks (N*b/t)" if world > 1
+                              else "queries per second",
+                "qps_global": round(b / (ms / 1e3), 1),
+            },
+            "roofline": roofline,
+            "roofline_other": roof_hbm if bound == "tensor" else roof_tc,
+            "kernel_ms": round(kern_avg, 4),
+            "e2e": {"value": round(e2e_value, 1), "unit": "QPS",
+                    "h2d_bytes_per_step": int(q_host.numel() * q_host.element_size()),
+                    "d2h_bytes_per_step": int(v_host.numel() * 4 + i_host.numel() * 8)},
+            "clocks": clk,
+            "gpu_launches": launches_per_step * args.steps,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(cfg)
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,396 @@
+// Host side of the C ABI declared in include/cvs.h: argument contracts,
+// launch planning, TMA descriptors, kernel launches and status reporting.
+//
+// The contracts mirror the reference's check_matrix / check_pair
+// (cuda_vector_search/csrc/kernels.cu:451-470) and fused_topk's k checks
+// (:509-510); the planner replaces its bq / chunk heuristics (:512-536), which
+// were tuned for a 40-SM T4, with one keyed on the B200's SM count: one CTA per
+// SM, query tiles of 128, corpus segments of whole 256-row tiles.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <climits>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "cvs.h"
+#include "cvs_kernels.h"
+
+namespace cvs {
+namespace {
+
+__device__ int g_device_error;  // one word per device; written by kernels on a failed wait
+
+thread_local std::string g_last_error;
+
+cvs_status fail(cvs_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+cvs_status fail(cvs_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+cvs_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(CVS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+  int* err = nullptr;  // device address of g_device_error
+};
+
+std::mutex g_mu;
+std::unordered_map<int, DeviceInfo> g_devices;
+cudaEvent_t g_prof_start = nullptr;
+cudaEvent_t g_prof_stop = nullptr;
+
+cvs_status device_info(DeviceInfo* out, int* dev_out = nullptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev_out) *dev_out = dev;
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_devices.find(dev);
+  if (it == g_devices.end()) {
+    DeviceInfo d;
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    if (d.major != 10 || d.minor != 0)
+      return fail(CVS_ERR_UNSUPPORTED,
+                  "device %d has compute capability %d.%d; this library is built for sm_100a (B200)",
+                  dev, d.major, d.minor);
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, g_device_error)) != cudaSuccess)
+      return cuda_fail(e, "cudaGetSymbolAddress(device error word)");
+    d.err = static_cast<int*>(p);
+    it = g_devices.emplace(dev, d).first;
+  }
+  *out = it->second;
+  return CVS_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 tensor [rows][cols], boxes of 64 columns x box_rows rows, 128-byte swizzle.
+cvs_status make_map(CUtensorMap* m, const void* base, int64_t rows, int cols, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(CVS_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CVS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return CVS_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cvs_status check_pair(const void* q, int64_t b, const void* x, int64_t n, int d_pad) {
+  if (b < 0 || b >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "query count %lld out of range", (long long)b);
+  if (n < 1 || n >= INT_MAX)
+    return fail(CVS_ERR_INVALID_ARGUMENT, "corpus must have 1 .. 2^31-1 rows (got %lld)", (long long)n);
+  if (d_pad < CVS_PAD || d_pad % CVS_PAD != 0)
+    return fail(CVS_ERR_INVALID_ARGUMENT, "width must be a positive multiple of 64 (zero-pad it); got %d", d_pad);
+  if (!x || !aligned16(x)) return fail(CVS_ERR_INVALID_ARGUMENT, "corpus must be a non-null 16-byte aligned pointer");
+  if (b > 0 && (!q || !aligned16(q)))
+    return fail(CVS_ERR_INVALID_ARGUMENT, "queries must be a non-null 16-byte aligned pointer");
+  return CVS_OK;
+}
+
+struct Plan {
+  bool gemv = false;
+  int epi = 0;
+  bool qres = false;
+  int qtiles = 0, segs = 0, tiles_per_seg = 0, ntiles = 0;
+  int cap = 0;
+  int rows_per_seg = 0;
+  size_t ws_bytes = 0;
+};
+
+constexpr size_t kWsAlign = 256;
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Corpus segmentation for the tcgen05 kernel: about one CTA per SM in total.
+void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks) {
+  p->qtiles = static_cast<int>((b + kTcM - 1) / kTcM);
+  p->ntiles = static_cast<int>((n + kTcN - 1) / kTcN);
+  int segs = chunks > 0 ? chunks : std::max(1, sms / std::max(1, p->qtiles));
+  segs = std::max(1, std::min(segs, p->ntiles));
+  p->tiles_per_seg = (p->ntiles + segs - 1) / segs;
+  p->segs = (p->ntiles + p->tiles_per_seg - 1) / p->tiles_per_seg;
+}
+
+cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const DeviceInfo& dev,
+                      Plan* p) {
+  if (k < 1 || k > CVS_MAX_FUSED_K)
+    return fail(CVS_ERR_INVALID_ARGUMENT, "fused top-k supports 1 <= k <= %d (got %d)", CVS_MAX_FUSED_K, k);
+  if (k > n) return fail(CVS_ERR_INVALID_ARGUMENT, "k (%d) must not exceed the corpus size (%lld)", k, (long long)n);
+  if (chunks < 0) return fail(CVS_ERR_INVALID_ARGUMENT, "chunks must be >= 0");
+  if (gemv_supported(static_cast<int>(b), k, d_pad)) {
+    p->gemv = true;
+    int segs = chunks > 0 ? chunks : dev.sms * gemv_blocks_per_sm(static_cast<int>(b), d_pad);
+    segs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(segs, n)));
+    p->rows_per_seg = static_cast<int>((n + segs - 1) / segs);
+    p->segs = static_cast<int>((n + p->rows_per_seg - 1) / p->rows_per_seg);
+    p->cap = k;
+    p->ws_bytes = round_up(static_cast<size_t>(b) * p->segs * p->cap * 8, kWsAlign);
+    return CVS_OK;
+  }
+  p->gemv = false;
+  plan_tc_grid(p, b, n, dev.sms, chunks);
+  if (k <= 16) {
+    p->epi = kEpiTopkReg16;
+    p->cap = k;
+  } else if (k <= 32) {
+    p->epi = kEpiTopkReg32;
+    p->cap = k;
+  } else {
+    p->epi = kEpiTopkBuf;
+    p->cap = static_cast<int>(round_up(static_cast<size_t>(std::max(2 * k, k + 32)), 32));
+  }
+  p->qres = (d_pad / kTcK) <= kTcMaxResidentSlices;
+  p->ws_bytes = round_up(static_cast<size_t>(b) * p->segs * p->cap * 8, kWsAlign);
+  return CVS_OK;
+}
+
+}  // namespace
+}  // namespace cvs
+
+using namespace cvs;
+
+extern "C" {
+
+const char* cvs_last_error(void) { return g_last_error.c_str(); }
+
+int cvs_abi_version(void) { return CVS_ABI_VERSION; }
+
+int cvs_pad_width(int d) { return d <= 0 ? 0 : (d + CVS_PAD - 1) / CVS_PAD * CVS_PAD; }
+
+cvs_status cvs_ingest(const void* src, int src_dtype, int64_t n, int d, int64_t src_row_stride,
+                      int d_pad, int cosine, void* dst_f16, void* stream) {
+  if (n < 0) return fail(CVS_ERR_INVALID_ARGUMENT, "row count must be >= 0");
+  if (n == 0) return CVS_OK;
+  if (!src || !dst_f16) return fail(CVS_ERR_INVALID_ARGUMENT, "null source or destination");
+  if (d < 1 || d > 2048) return fail(CVS_ERR_INVALID_ARGUMENT, "width must be in 1 .. 2048 (got %d)", d);
+  if (d_pad < d || d_pad % CVS_PAD != 0)
+    return fail(CVS_ERR_INVALID_ARGUMENT, "d_pad (%d) must be a multiple of 64 and >= d (%d)", d_pad, d);
+  if (src_row_stride < d) return fail(CVS_ERR_INVALID_ARGUMENT, "source row stride smaller than the width");
+  if (src_dtype < CVS_F32 || src_dtype > CVS_F64) return fail(CVS_ERR_INVALID_ARGUMENT, "unknown source dtype %d", src_dtype);
+  if (src == dst_f16 && !(src_dtype == CVS_F16 && d == d_pad && src_row_stride == d_pad))
+    return fail(CVS_ERR_INVALID_ARGUMENT, "in-place ingest needs fp16 input with d == d_pad == stride");
+  DeviceInfo dev;
+  cvs_status st = device_info(&dev);
+  if (st != CVS_OK) return st;
+  cudaError_t e = ingest_launch(src, src_dtype, n, d, src_row_stride, d_pad, cosine,
+                                static_cast<__half*>(dst_f16), dev.sms, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "ingest launch");
+  return CVS_OK;
+}
+
+cvs_status cvs_fused_topk_workspace_size(int64_t b, int64_t n, int d_pad, int k, int plan_bq,
+                                         int plan_chunks, size_t* bytes) {
+  (void)plan_bq;
+  if (!bytes) return fail(CVS_ERR_INVALID_ARGUMENT, "bytes must not be null");
+  *bytes = 0;
+  if (b < 0 || b >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "query count out of range");
+  if (n < 1 || n >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "corpus must have 1 .. 2^31-1 rows");
+  if (d_pad < CVS_PAD || d_pad % CVS_PAD != 0) return fail(CVS_ERR_INVALID_ARGUMENT, "width must be a multiple of 64");
+  if (b == 0) return CVS_OK;
+  DeviceInfo dev;
+  cvs_status st = device_info(&dev);
+  if (st != CVS_OK) return st;
+  Plan p;
+  st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p);
+  if (st != CVS_OK) return st;
+  *bytes = p.ws_bytes;
+  return CVS_OK;
+}
+
+cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64_t n, int d_pad,
+                          int k, int64_t id_offset, float* out_scores, int64_t* out_ids,
+                          void* workspace, size_t workspace_bytes, int plan_bq, int plan_chunks,
+                          int64_t* plan_out, void* stream) {
+  cvs_status st = check_pair(q_f16, b, x_f16, n, d_pad);
+  if (st != CVS_OK) return st;
+  DeviceInfo dev;
+  if ((st = device_info(&dev)) != CVS_OK) return st;
+  Plan p;
+  if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p)) != CVS_OK) return st;
+  if (plan_out) {
+    plan_out[0] = plan_bq > 0 ? plan_bq : (p.gemv ? static_cast<int64_t>(b) : static_cast<int64_t>(kTcM));
+    plan_out[1] = p.segs;
+  }
+  if (b == 0) return CVS_OK;
+  if (!out_scores || !out_ids) return fail(CVS_ERR_INVALID_ARGUMENT, "null output pointer");
+  if (!workspace || workspace_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) != 0)
+    return fail(CVS_ERR_WORKSPACE, "workspace of %zu bytes (256-byte aligned) required, got %zu at %p",
+                p.ws_bytes, workspace_bytes, workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint64_t* part = static_cast<uint64_t*>(workspace);
+  const bool prof = g_prof_start && g_prof_stop;
+  cudaError_t e;
+  if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
+  if (p.gemv) {
+    GemvArgs a{};
+    a.x = static_cast<const __half*>(x_f16);
+    a.q = static_cast<const __half*>(q_f16);
+    a.b = static_cast<int>(b);
+    a.n = static_cast<int>(n);
+    a.d_pad = d_pad;
+    a.k = k;
+    a.segs = p.segs;
+    a.rows_per_seg = p.rows_per_seg;
+    a.part = part;
+    a.err = dev.err;
+    if ((e = gemv_launch(a, s)) != cudaSuccess) return cuda_fail(e, "gemv top-k launch");
+  } else {
+    CUtensorMap qmap, xmap;
+    if ((st = make_map(&qmap, q_f16, b, d_pad, kTcM)) != CVS_OK) return st;
+    if ((st = make_map(&xmap, x_f16, n, d_pad, kTcN)) != CVS_OK) return st;
+    TcArgs a{};
+    a.b = static_cast<int>(b);
+    a.n = static_cast<int>(n);
+    a.d_pad = d_pad;
+    a.ksl = d_pad / kTcK;
+    a.qtiles = p.qtiles;
+    a.segs = p.segs;
+    a.tiles_per_seg = p.tiles_per_seg;
+    a.ntiles = p.ntiles;
+    a.k = k;
+    a.cap = p.cap;
+    a.part = part;
+    a.err = dev.err;
+    if ((e = tc_launch(p.epi, p.qres, &qmap, &xmap, a, s)) != cudaSuccess)
+      return cuda_fail(e, "tcgen05 search launch");
+  }
+  if (prof && (e = cudaEventRecord(g_prof_stop, s)) != cudaSuccess) return cuda_fail(e, "profile event");
+  MergeKeysArgs m{};
+  m.part = part;
+  m.b = static_cast<int>(b);
+  m.lists = p.segs;
+  m.stride = p.cap;
+  m.per_list = k;
+  m.k = k;
+  m.id_offset = id_offset;
+  m.out_v = out_scores;
+  m.out_i = reinterpret_cast<long long*>(out_ids);
+  m.err = dev.err;
+  if ((e = merge_keys_launch(m, s)) != cudaSuccess) return cuda_fail(e, "merge launch");
+  return CVS_OK;
+}
+
+cvs_status cvs_scores(const void* q_f16, int64_t b, const void* x_f16, int64_t n, int d_pad,
+                      void* out, int out_fp32, void* stream) {
+  cvs_status st = check_pair(q_f16, b, x_f16, n, d_pad);
+  if (st != CVS_OK) return st;
+  if (b == 0) return CVS_OK;
+  if (!out) return fail(CVS_ERR_INVALID_ARGUMENT, "null output pointer");
+  DeviceInfo dev;
+  if ((st = device_info(&dev)) != CVS_OK) return st;
+  Plan p;
+  plan_tc_grid(&p, b, n, dev.sms, 0);
+  CUtensorMap qmap, xmap;
+  if ((st = make_map(&qmap, q_f16, b, d_pad, kTcM)) != CVS_OK) return st;
+  if ((st = make_map(&xmap, x_f16, n, d_pad, kTcN)) != CVS_OK) return st;
+  TcArgs a{};
+  a.b = static_cast<int>(b);
+  a.n = static_cast<int>(n);
+  a.d_pad = d_pad;
+  a.ksl = d_pad / kTcK;
+  a.qtiles = p.qtiles;
+  a.segs = p.segs;
+  a.tiles_per_seg = p.tiles_per_seg;
+  a.ntiles = p.ntiles;
+  a.k = 1;
+  a.cap = 1;
+  a.scores_out = out;
+  a.err = dev.err;
+  const bool qres = (d_pad / kTcK) <= kTcMaxResidentSlices;
+  cudaError_t e = tc_launch(out_fp32 ? kEpiStoreF32 : kEpiStoreF16, qres, &qmap, &xmap, a,
+                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 score launch");
+  return CVS_OK;
+}
+
+cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t lists, int64_t b,
+                           int64_t len, int k, float* out_scores, int64_t* out_ids, void* stream) {
+  if (lists < 1 || b < 0 || len < 1 || lists * len >= INT_MAX)
+    return fail(CVS_ERR_INVALID_ARGUMENT, "bad list shape [%lld][%lld][%lld]", (long long)lists,
+                (long long)b, (long long)len);
+  if (k < 1 || k > CVS_MAX_FUSED_K) return fail(CVS_ERR_INVALID_ARGUMENT, "k out of range (%d)", k);
+  if (b == 0) return CVS_OK;
+  if (!scores || !ids || !out_scores || !out_ids) return fail(CVS_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo dev;
+  cvs_status st = device_info(&dev);
+  if (st != CVS_OK) return st;
+  MergeListsArgs a{};
+  a.v = scores;
+  a.ids = reinterpret_cast<const long long*>(ids);
+  a.b = static_cast<int>(b);
+  a.lists = static_cast<int>(lists);
+  a.len = static_cast<int>(len);
+  a.k = k;
+  a.out_v = out_scores;
+  a.out_i = reinterpret_cast<long long*>(out_ids);
+  a.err = dev.err;
+  cudaError_t e = merge_lists_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return CVS_OK;
+}
+
+cvs_status cvs_poll_device_error(int device, int* code) {
+  if (!code) return fail(CVS_ERR_INVALID_ARGUMENT, "code must not be null");
+  *code = 0;
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  DeviceInfo dev;
+  cvs_status st = device_info(&dev);
+  if (st == CVS_OK) {
+    int zero = 0;
+    if ((e = cudaMemcpy(code, dev.err, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess ||
+        (e = cudaMemcpy(dev.err, &zero, sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess)
+      st = cuda_fail(e, "reading the device error word");
+  }
+  cudaSetDevice(prev);
+  if (st != CVS_OK) return st;
+  if (*code != 0)
+    return fail(CVS_ERR_DEVICE_TIMEOUT, "a kernel gave up waiting on its pipeline (code 0x%x)", *code);
+  return CVS_OK;
+}
+
+cvs_status cvs_set_profile_events(void* start_event, void* stop_event) {
+  g_prof_start = static_cast<cudaEvent_t>(start_event);
+  g_prof_stop = static_cast<cudaEvent_t>(stop_event);
+  return CVS_OK;
+}
+
+}  // extern "C"

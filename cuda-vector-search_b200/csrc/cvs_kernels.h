@@ -1,0 +1,104 @@
+// Launch-side declarations shared by the kernel translation units and the
+// C-ABI host code (cvs_capi.cu). Nothing here is part of the public ABI; the
+// public entry points are declared in include/cvs.h.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace cvs {
+
+// ---- tcgen05 fused score + top-k / score-store kernel ----------------------
+constexpr int kTcM = 128;          // queries per tile (MMA M; TMEM lanes)
+constexpr int kTcN = 256;          // corpus rows per tile (MMA N; TMEM columns)
+constexpr int kTcK = 64;           // halves per K slice (one 128-byte swizzled row)
+constexpr int kTcThreads = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kTcStages = 4;
+constexpr int kTcMaxResidentSlices = 7;  // queries stay in smem when d_pad <= 448
+
+enum TcEpilogue : int {
+  kEpiTopkReg16 = 0,   // k <= 16: per-query sorted list in registers
+  kEpiTopkReg32 = 1,   // k <= 32
+  kEpiTopkBuf = 2,     // k  > 32: per-query candidate buffer in global memory
+  kEpiStoreF32 = 3,    // write the score matrix as fp32
+  kEpiStoreF16 = 4,    // write the score matrix as fp16
+};
+
+struct TcArgs {
+  int b;              // queries
+  int n;              // corpus rows
+  int d_pad;          // row width in halves (multiple of 64)
+  int ksl;            // d_pad / 64
+  int qtiles;         // ceil(b / 128)
+  int segs;           // corpus segments (each a contiguous run of 256-row tiles)
+  int tiles_per_seg;
+  int ntiles;         // ceil(n / 256)
+  int k;              // candidates kept per (query, segment)
+  int cap;            // slots per (query, segment) list; cap >= k
+  uint64_t* part;     // [b][segs][cap] ordered keys
+  void* scores_out;   // [b][n] fp32/fp16 for the store epilogues
+  int* err;           // device error word
+};
+
+size_t tc_smem_bytes(bool resident_queries, int ksl);
+cudaError_t tc_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
+                      const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
+
+// ---- CUDA-core GEMV + top-k for batches of at most 8 queries ---------------
+constexpr int kGemvThreads = 256;
+constexpr int kGemvMaxK = 32;
+
+struct GemvArgs {
+  const __half* x;    // [n][d_pad]
+  const __half* q;    // [b][d_pad]
+  int b;
+  int n;
+  int d_pad;
+  int k;
+  int segs;           // grid size; segment s covers rows [s*rows_per_seg, ...)
+  int rows_per_seg;
+  uint64_t* part;     // [b][segs][k]
+  int* err;
+};
+
+bool gemv_supported(int b, int k, int d_pad);
+cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t stream);
+int gemv_blocks_per_sm(int b, int d_pad);
+
+// ---- merge of per-segment candidate lists into the final sorted top-k ------
+struct MergeKeysArgs {
+  const uint64_t* part;  // [b][lists][stride], first per_list entries of each used
+  int b;
+  int lists;
+  int stride;
+  int per_list;
+  int k;
+  long long id_offset;   // added to every returned row id
+  float* out_v;          // [b][k]
+  long long* out_i;      // [b][k]
+  int* err;
+};
+cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream);
+
+struct MergeListsArgs {
+  const float* v;        // [lists][b][len] scores
+  const long long* ids;  // [lists][b][len] ids (must lie in [0, 2^31))
+  int b;
+  int lists;
+  int len;
+  int k;
+  float* out_v;          // [b][k]
+  long long* out_i;      // [b][k]
+  int* err;
+};
+cudaError_t merge_lists_launch(const MergeListsArgs& a, cudaStream_t stream);
+
+// ---- ingest: dtype conversion, optional L2 normalisation, width padding ----
+enum SrcDtype : int { kSrcF32 = 0, kSrcF16 = 1, kSrcBF16 = 2, kSrcF64 = 3 };
+cudaError_t ingest_launch(const void* src, int src_dtype, long long n, int d, long long src_stride,
+                          int d_pad, int cosine, __half* dst, int num_sms, cudaStream_t stream);
+
+}  // namespace cvs

@@ -1,0 +1,128 @@
+// Warp-cooperative selection over ordered 64-bit candidate keys (see make_key
+// in cvs_device.cuh: larger key = higher score, ties broken by the smaller row).
+//
+// warp_kth_key finds the k-th largest of m unique keys with an MSB-first radix
+// select (8-bit digits, one 256-bin shared-memory histogram per warp). It stops
+// as soon as the bucket holding the k-th key is fully selected, so on real
+// score distributions it takes 2-4 passes over the keys instead of 8.
+//
+// This replaces the reference's per-lane replace-the-minimum list
+// (cuda_vector_search/csrc/kernels.cu:187-275) for every list longer than a
+// warp: per-chunk candidate lists, per-query candidate buffers and the final
+// cross-chunk merge.
+#pragma once
+
+#include <cstdint>
+
+namespace cvs {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+__device__ __forceinline__ uint64_t shfl_u64(uint64_t v, int src) {
+  const uint32_t lo = __shfl_sync(kFullMask, static_cast<uint32_t>(v), src);
+  const uint32_t hi = __shfl_sync(kFullMask, static_cast<uint32_t>(v >> 32), src);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+__device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const uint64_t o = shfl_u64(v, (threadIdx.x & 31) ^ off);
+    v = o < v ? o : v;
+  }
+  return v;
+}
+
+// Key accessor over a contiguous array (shared or global memory).
+struct ContigKeys {
+  const uint64_t* p;
+  __device__ __forceinline__ uint64_t operator()(int i) const { return p[i]; }
+};
+
+// Returns the k-th largest of the m keys produced by acc(0..m-1). Requires
+// 1 <= k <= m and unique keys. `hist` is this warp's 256-entry shared scratch.
+// Must be called by all 32 lanes of the warp with identical arguments.
+template <class Acc>
+__device__ uint64_t warp_kth_key(const Acc& acc, int m, int k, uint32_t* hist, int lane) {
+  uint64_t prefix = 0;
+  uint64_t pmask = 0;
+  int want = k;  // rank of the target among keys that match `prefix`
+#pragma unroll 1
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = lane; i < 256; i += 32) hist[i] = 0u;
+    __syncwarp();
+    for (int i = lane; i < m; i += 32) {
+      const uint64_t key = acc(i);
+      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    // Lane l owns bins 255-8l .. 248-8l, visited from the highest digit down.
+    uint32_t c[8];
+    uint32_t tot = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = hist[255 - 8 * lane - j];
+      tot += c[j];
+    }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t v = __shfl_up_sync(kFullMask, incl, off);
+      if (lane >= off) incl += v;
+    }
+    const uint32_t excl = incl - tot;
+    const bool mine = excl < static_cast<uint32_t>(want) && static_cast<uint32_t>(want) <= incl;
+    const unsigned owner = __ballot_sync(kFullMask, mine);
+    int digit = 0;
+    uint32_t above = 0, in_bin = 0;
+    if (mine) {
+      uint32_t run = excl;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (in_bin == 0 && run + c[j] >= static_cast<uint32_t>(want)) {
+          digit = 255 - 8 * lane - j;
+          above = run;
+          in_bin = c[j];
+        }
+        run += c[j];
+      }
+    }
+    const int src = __ffs(owner) - 1;
+    digit = __shfl_sync(kFullMask, digit, src);
+    above = __shfl_sync(kFullMask, above, src);
+    in_bin = __shfl_sync(kFullMask, in_bin, src);
+    want -= static_cast<int>(above);
+    prefix |= static_cast<uint64_t>(digit) << shift;
+    pmask |= static_cast<uint64_t>(255u) << shift;
+    if (in_bin == static_cast<uint32_t>(want)) {
+      // Every key in this bucket is selected: the k-th key is its smallest.
+      uint64_t mn = ~0ull;
+      for (int i = lane; i < m; i += 32) {
+        const uint64_t key = acc(i);
+        if ((key & pmask) == prefix && key < mn) mn = key;
+      }
+      __syncwarp();
+      return warp_min_u64(mn);
+    }
+  }
+  __syncwarp();
+  return prefix;  // all 64 bits fixed: this is the k-th key itself
+}
+
+// Keeps, in place and in their original order, the keys of list[0..m) that are
+// >= kth. Returns how many were kept. Whole warp.
+__device__ __forceinline__ int warp_compact_ge(uint64_t* list, int m, uint64_t kth, int lane) {
+  int base = 0;
+  for (int i0 = 0; i0 < m; i0 += 32) {
+    const int i = i0 + lane;
+    const uint64_t key = i < m ? list[i] : 0ull;
+    const bool keep = i < m && key >= kth;
+    const unsigned bal = __ballot_sync(kFullMask, keep);
+    if (keep) list[base + __popc(bal & ((1u << lane) - 1u))] = key;
+    base += __popc(bal);
+  }
+  __syncwarp();
+  return base;
+}
+
+}  // namespace cvs

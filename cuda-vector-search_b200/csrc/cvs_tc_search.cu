@@ -1,0 +1,510 @@
+// tcgen05 score kernel with fused per-query top-k (or score-store) epilogue.
+//
+// Replaces the reference's WMMA tile + fused top-k kernel
+// (cuda_vector_search/csrc/kernels.cu:123-177 score_tile, :313-371
+// fused_topk_kernel) and its full-matrix score kernel (:285-311).
+//
+// Operand orientation: A = a 128-query tile (MMA M, TMEM lanes), B = a 256-row
+// corpus tile (MMA N, TMEM columns), both K-major fp16 with the 128-byte
+// swizzle, fp32 accumulation in TMEM. Thread i of epilogue warp w therefore
+// reads, with one tcgen05.ld, 32 consecutive corpus scores of ONE query and can
+// run that query's top-k on its own, with no cross-lane traffic.
+//
+// Grid: one CTA per (query tile, corpus segment); the CTAs of one segment are
+// adjacent in launch order so they stream the same corpus tiles at the same
+// time and the second read of a tile hits L2. Each CTA: warp 0 issues TMA,
+// warp 1 issues tcgen05.mma (one elected thread each), warps 2-5 drain two
+// double-buffered 128x256 fp32 accumulators (all 512 TMEM columns).
+// Corpus slices stream through a ring of stages; the query tile either stays
+// resident in shared memory for the whole kernel (d_pad <= 448, 3 stages) or
+// streams beside each corpus slice (it is L2 resident; 4 stages).
+#include <type_traits>
+
+#include "cvs_device.cuh"
+#include "cvs_kernels.h"
+#include "cvs_select.cuh"
+
+namespace cvs {
+
+namespace {
+
+constexpr int kQSliceBytes = kTcM * kTcK * 2;  // 16 KB
+constexpr int kXSliceBytes = kTcN * kTcK * 2;  // 32 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr int kEpiWarps = 4;
+
+// Resident queries leave room for 3 corpus stages (96 KB in flight, enough to
+// cover HBM latency); streamed queries use 4 stages of 48 KB.
+__host__ __device__ constexpr int num_stages(bool qres) { return qres ? 3 : 4; }
+
+// Shared-memory carve-up (offsets from a 1024-byte aligned base).
+struct Layout {
+  int q_res;      // resident query slices
+  int stages;     // ring of stages
+  int stage_bytes;
+  int bars;       // mbarriers
+  int hist;       // per epilogue warp radix histograms
+  int total;
+};
+
+__host__ __device__ constexpr Layout make_layout(bool qres, int ksl) {
+  Layout l{};
+  l.q_res = 0;
+  l.stage_bytes = qres ? kXSliceBytes : (kXSliceBytes + kQSliceBytes);
+  l.stages = qres ? ksl * kQSliceBytes : 0;
+  l.bars = l.stages + num_stages(qres) * l.stage_bytes;
+  // full[4], empty[4], tfull[2], tempty[2], qfull, done, tmem holder, abort
+  l.hist = l.bars + 8 * (2 * kTcStages + 6) + 16;
+  l.total = l.hist + kEpiWarps * 256 * 4;
+  return l;
+}
+
+struct Shared {
+  uint8_t* base;
+  Layout l;
+  __device__ uint8_t* qres(int ks) const { return base + l.q_res + ks * kQSliceBytes; }
+  __device__ uint8_t* stage_x(int s) const { return base + l.stages + s * l.stage_bytes; }
+  __device__ uint8_t* stage_q(int s) const {
+    return base + l.stages + s * l.stage_bytes + kXSliceBytes;
+  }
+  __device__ uint64_t* bar(int i) const { return reinterpret_cast<uint64_t*>(base + l.bars) + i; }
+  __device__ uint64_t* full(int s) const { return bar(s); }
+  __device__ uint64_t* empty(int s) const { return bar(kTcStages + s); }
+  __device__ uint64_t* tfull(int a) const { return bar(2 * kTcStages + a); }
+  __device__ uint64_t* tempty(int a) const { return bar(2 * kTcStages + 2 + a); }
+  __device__ uint64_t* qfull() const { return bar(2 * kTcStages + 4); }
+  __device__ uint64_t* done() const { return bar(2 * kTcStages + 5); }
+  __device__ uint32_t* tmem_holder() const {
+    return reinterpret_cast<uint32_t*>(base + l.bars + 8 * (2 * kTcStages + 6));
+  }
+  __device__ volatile int* abort_flag() const {
+    return reinterpret_cast<volatile int*>(base + l.bars + 8 * (2 * kTcStages + 6) + 4);
+  }
+  __device__ uint32_t* hist(int w) const {
+    return reinterpret_cast<uint32_t*>(base + l.hist) + 256 * w;
+  }
+};
+
+// Bounded wait that ignores the abort flag; used only to drain work that was
+// already issued before leaving on an error path.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues. consume() sees 32 consecutive corpus scores of this thread's
+// query (rows row0 .. row0+31, of which the first `nvalid` exist).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ bool any_above(const uint32_t (&r)[32], float thr) {
+  bool any = false;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) any |= __uint_as_float(r[j]) > thr;
+  return any;
+}
+
+// Bit j set when score j exceeds thr (only the first nvalid scores count).
+__device__ __forceinline__ uint32_t above_mask(const uint32_t (&r)[32], float thr, int nvalid) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) m |= (__uint_as_float(r[j]) > thr ? 1u : 0u) << j;
+  return nvalid >= 32 ? m : (m & ((1u << nvalid) - 1u));
+}
+
+// r[j] for a run-time j without indexing the register array (which would move
+// it to local memory).
+__device__ __forceinline__ float pick(const uint32_t (&r)[32], int j) {
+  uint32_t v = r[0];
+#pragma unroll
+  for (int t = 1; t < 32; ++t) v = (t == j) ? r[t] : v;
+  return __uint_as_float(v);
+}
+
+// Sorted (score desc, row asc) list of KP slots in registers holding the best
+// k <= KP candidates in its LAST k slots; the first KP-k slots are parked at
+// +inf so no finite score displaces them. The k-th best is then always the
+// last slot (a run-time slot index would push the list to local memory).
+template <int KP>
+struct EpiTopkReg {
+  float tv[KP];
+  uint32_t ti[KP];
+  float thr;
+  int k;
+
+  __device__ __forceinline__ void init(const TcArgs& a) {
+    k = a.k;
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      tv[j] = (j < KP - k) ? INFINITY : -INFINITY;
+      ti[j] = 0xFFFFFFFFu;
+    }
+    thr = -INFINITY;
+  }
+
+  __device__ __forceinline__ void insert(float s, uint32_t row) {
+    float cs = s;
+    uint32_t ci = row;
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      const bool sw = (cs > tv[j]) || (cs == tv[j] && ci < ti[j]);
+      const float ov = tv[j];
+      const uint32_t oi = ti[j];
+      tv[j] = sw ? cs : ov;
+      ti[j] = sw ? ci : oi;
+      cs = sw ? ov : cs;
+      ci = sw ? oi : ci;
+    }
+    thr = tv[KP - 1];
+  }
+
+  __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
+                                          bool qvalid, const Shared&, int) {
+    if (!qvalid || !any_above(r, thr)) return;
+    uint32_t m = above_mask(r, thr, nvalid);
+    while (m) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      const float s = pick(r, j);
+      if (s > thr) insert(s, static_cast<uint32_t>(row0 + j));
+    }
+  }
+
+  __device__ __forceinline__ void finish(const TcArgs& a, int q, int seg, bool qvalid, const Shared&, int) {
+    if (!qvalid) return;
+    uint64_t* out = a.part + (static_cast<size_t>(q) * a.segs + seg) * a.cap;
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      if (j >= KP - k) out[j - (KP - k)] = (tv[j] == -INFINITY) ? 0ull : make_key(tv[j], ti[j]);
+    }
+  }
+};
+
+// Per-query candidate buffer of `cap` keys in global memory (L2 resident).
+// A key is appended when its score beats the current k-th best; when a list
+// could overflow on the next chunk, the warp cooperatively keeps its top k.
+struct EpiTopkBuf {
+  uint64_t* list;
+  int cnt;
+  float thr;
+
+  __device__ __forceinline__ void init(const TcArgs&) {
+    list = nullptr;
+    cnt = 0;
+    thr = -INFINITY;
+  }
+
+  __device__ __forceinline__ void compact_lanes(unsigned need, const TcArgs& a, const Shared& sh,
+                                                int ew, int lane) {
+    while (need) {
+      const int src = __ffs(need) - 1;
+      need &= need - 1;
+      uint64_t* L = reinterpret_cast<uint64_t*>(shfl_u64(reinterpret_cast<uint64_t>(list), src));
+      const int m = __shfl_sync(kFullMask, cnt, src);
+      const uint64_t kth = warp_kth_key(ContigKeys{L}, m, a.k, sh.hist(ew), lane);
+      warp_compact_ge(L, m, kth, lane);
+      if (lane == src) {
+        cnt = a.k;
+        thr = key_score(kth);
+      }
+    }
+  }
+
+  __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
+                                          bool qvalid, const Shared& sh, int ew) {
+    // `list` is set lazily so the pointer math stays out of the hot loop.
+    if (qvalid && any_above(r, thr)) {
+      uint32_t m = above_mask(r, thr, nvalid);
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        list[cnt++] = make_key(pick(r, j), static_cast<uint32_t>(row0 + j));
+      }
+    }
+    (void)sh;
+    (void)ew;
+  }
+
+  __device__ __forceinline__ void finish(const TcArgs& a, int, int, bool qvalid, const Shared& sh, int ew) {
+    const int lane = threadIdx.x & 31;
+    compact_lanes(__ballot_sync(kFullMask, qvalid && cnt > a.k), a, sh, ew, lane);
+    if (qvalid) {
+      for (int j = cnt; j < a.k; ++j) list[j] = 0ull;
+    }
+  }
+};
+
+// Writes the score tile to [b][n] (fp32 or fp16).
+template <bool F32>
+struct EpiStore {
+  __device__ __forceinline__ void init(const TcArgs&) {}
+  __device__ __forceinline__ void consume_store(const uint32_t (&r)[32], int row0, int nvalid,
+                                                bool qvalid, const TcArgs& a, int q) {
+    if (!qvalid) return;
+    const size_t o = static_cast<size_t>(q) * a.n + row0;
+    if (F32) {
+      float* dst = reinterpret_cast<float*>(a.scores_out) + o;
+      if (nvalid == 32 && (o & 3) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nvalid) dst[j] = __uint_as_float(r[j]);
+      }
+    } else {
+      __half* dst = reinterpret_cast<__half*>(a.scores_out) + o;
+      if (nvalid == 32 && (o & 7) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const __half2 h = __floats2half2_rn(__uint_as_float(r[j + 2 * t]),
+                                                __uint_as_float(r[j + 2 * t + 1]));
+            w[t] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(dst + j) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nvalid) dst[j] = __float2half_rn(__uint_as_float(r[j]));
+      }
+    }
+  }
+};
+
+template <class E>
+struct is_store : std::false_type {};
+template <bool F>
+struct is_store<EpiStore<F>> : std::true_type {};
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <bool QRES, class Epi>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_search_kernel(const __grid_constant__ CUtensorMap qmap,
+                     const __grid_constant__ CUtensorMap xmap, const TcArgs a) {
+  constexpr int kS = num_stages(QRES);  // ring depth (barrier arrays are sized for the max)
+  extern __shared__ uint8_t smem_raw[];
+  Shared sh;
+  sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~static_cast<uintptr_t>(1023));
+  sh.l = make_layout(QRES, a.ksl);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qt = blockIdx.x % a.qtiles;
+  const int seg = blockIdx.x / a.qtiles;
+  const int t_begin = seg * a.tiles_per_seg;
+  const int t_end = min(a.ntiles, t_begin + a.tiles_per_seg);
+  const int ntl = max(0, t_end - t_begin);
+  volatile int* abort = sh.abort_flag();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kS; ++s) {
+      mbar_init(sh.full(s), 1);
+      mbar_init(sh.empty(s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(sh.tfull(t), 1);
+      mbar_init(sh.tempty(t), kEpiWarps);
+    }
+    mbar_init(sh.qfull(), 1);
+    mbar_init(sh.done(), 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&qmap);
+    tma_prefetch_desc(&xmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(sh.tmem_holder(), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *sh.tmem_holder();
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (elect_one_lane()) {
+      const uint64_t pol_x = l2_policy_evict_first();
+      const uint64_t pol_q = l2_policy_evict_last();
+      const int qrow0 = qt * kTcM;
+      if (QRES) {
+        mbar_arrive_expect_tx(sh.qfull(), static_cast<uint32_t>(a.ksl * kQSliceBytes));
+        for (int ks = 0; ks < a.ksl; ++ks)
+          tma_load_2d(sh.qres(ks), &qmap, sh.qfull(), ks * kTcK, qrow0, pol_q);
+      }
+      const uint32_t tx = QRES ? kXSliceBytes : (kXSliceBytes + kQSliceBytes);
+      int it = 0;
+      bool ok = true;
+      for (int t = 0; t < ntl && ok; ++t) {
+        const int row0 = (t_begin + t) * kTcN;
+        for (int ks = 0; ks < a.ksl; ++ks, ++it) {
+          const int s = it % kS;
+          const uint32_t ph = (it / kS) & 1;
+          if (!mbar_wait(sh.empty(s), ph ^ 1, abort, a.err, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(sh.full(s), tx);
+          tma_load_2d(sh.stage_x(s), &xmap, sh.full(s), ks * kTcK, row0, pol_x);
+          if (!QRES) tma_load_2d(sh.stage_q(s), &qmap, sh.full(s), ks * kTcK, qrow0, pol_q);
+        }
+      }
+      if (!ok) {
+        // Leaving early: let every copy already issued land before the CTA exits.
+        for (int j = max(0, it - kS); j < it; ++j)
+          mbar_wait_drain(sh.full(j % kS), (j / kS) & 1);
+        if (QRES) mbar_wait_drain(sh.qfull(), 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (elect_one_lane()) {
+      const uint32_t idesc = idesc_f16_f32(kTcM, kTcN);
+      bool ok = true;
+      if (QRES) ok = mbar_wait(sh.qfull(), 0, abort, a.err, 2);
+      int it = 0;
+      for (int t = 0; t < ntl && ok; ++t) {
+        const int acc = t & 1;
+        const uint32_t use = static_cast<uint32_t>(t >> 1);
+        if (!mbar_wait(sh.tempty(acc), (use & 1) ^ 1, abort, a.err, 3)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTcN);
+        for (int ks = 0; ks < a.ksl; ++ks, ++it) {
+          const int s = it % kS;
+          const uint32_t ph = (it / kS) & 1;
+          if (!mbar_wait(sh.full(s), ph, abort, a.err, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t qa = smem_u32(QRES ? sh.qres(ks) : sh.stage_q(s));
+          const uint32_t xa = smem_u32(sh.stage_x(s));
+#pragma unroll
+          for (int kk = 0; kk < kTcK / 16; ++kk) {
+            tc_mma_f16(d_tmem, smem_desc_sw128(qa + kk * 32), smem_desc_sw128(xa + kk * 32), idesc,
+                       (ks | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(sh.empty(s));
+        }
+        if (!ok) break;
+        tc_commit(sh.tfull(acc));
+      }
+      // Every MMA must retire before the accumulators are released.
+      tc_commit(sh.done());
+      mbar_wait_drain(sh.done(), 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ----------------------------------
+    const int ew = warp - 2;             // 0..3
+    const int quad = warp & 3;           // TMEM lane quadrant this warp may access
+    const int q = qt * kTcM + quad * 32 + lane;
+    const bool qvalid = q < a.b;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    Epi epi;
+    epi.init(a);
+    if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
+      if (qvalid) epi.list = a.part + (static_cast<size_t>(q) * a.segs + seg) * a.cap;
+    }
+    bool ok = true;
+    for (int t = 0; t < ntl; ++t) {
+      const int acc = t & 1;
+      const uint32_t use = static_cast<uint32_t>(t >> 1);
+      if (!mbar_wait(sh.tfull(acc), use & 1, abort, a.err, 5)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int row0 = (t_begin + t) * kTcN;
+      const int valid = min(kTcN, a.n - row0);
+      for (int c = 0; c < kTcN / 32; ++c) {
+        if (c * 32 >= valid) break;
+        uint32_t r[32];
+        tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(acc * kTcN + c * 32), r);
+        tmem_wait_ld();
+        const int nv = min(32, valid - c * 32);
+        if constexpr (is_store<Epi>::value) {
+          epi.consume_store(r, row0 + c * 32, nv, qvalid, a, q);
+        } else {
+          epi.consume(r, row0 + c * 32, nv, qvalid, sh, ew);
+          if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
+            epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a, sh, ew,
+                              lane);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sh.tempty(acc));
+    }
+    if constexpr (!is_store<Epi>::value) {
+      if (ok) epi.finish(a, q, seg, qvalid, sh, ew);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <bool QRES, class Epi>
+cudaError_t launch_one(const CUtensorMap* qmap, const CUtensorMap* xmap, const TcArgs& a,
+                       cudaStream_t stream) {
+  const Layout l = make_layout(QRES, a.ksl);
+  const size_t smem = static_cast<size_t>(l.total) + 1024;
+  auto kern = tc_search_kernel<QRES, Epi>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const unsigned grid = static_cast<unsigned>(a.qtiles) * static_cast<unsigned>(a.segs);
+  kern<<<grid, kTcThreads, smem, stream>>>(*qmap, *xmap, a);
+  return cudaGetLastError();
+}
+
+template <bool QRES>
+cudaError_t launch_epi(int epi, const CUtensorMap* qmap, const CUtensorMap* xmap, const TcArgs& a,
+                       cudaStream_t stream) {
+  switch (epi) {
+    case kEpiTopkReg16: return launch_one<QRES, EpiTopkReg<16>>(qmap, xmap, a, stream);
+    case kEpiTopkReg32: return launch_one<QRES, EpiTopkReg<32>>(qmap, xmap, a, stream);
+    case kEpiTopkBuf: return launch_one<QRES, EpiTopkBuf>(qmap, xmap, a, stream);
+    case kEpiStoreF32: return launch_one<QRES, EpiStore<true>>(qmap, xmap, a, stream);
+    case kEpiStoreF16: return launch_one<QRES, EpiStore<false>>(qmap, xmap, a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+size_t tc_smem_bytes(bool resident_queries, int ksl) {
+  return static_cast<size_t>(make_layout(resident_queries, ksl).total) + 1024;
+}
+
+cudaError_t tc_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
+                      const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream) {
+  if (resident_queries && a.ksl > kTcMaxResidentSlices) return cudaErrorInvalidValue;
+  return resident_queries ? launch_epi<true>(epi, qmap, xmap, a, stream)
+                          : launch_epi<false>(epi, qmap, xmap, a, stream);
+}
+
+}  // namespace cvs

@@ -1,0 +1,193 @@
+"""Exact top-k search over an fp16 embedding matrix held on one B200.
+
+Same public API as the reference's ``cuda_vector_search.Index``
+(cuda_vector_search/index.py:44-155): constructor arguments, ``search``,
+``scores``, ``save`` / ``load``, ``len()``, ``.dim``, ``.embeddings``. What changes
+underneath:
+
+* storage: one ingest kernel converts to fp16, L2-normalises (cosine) and pads
+  the width to a multiple of 64 in a single pass (index.py:35-41 + 27-32 there);
+* search: ``method="fused"`` (the default) runs the tcgen05 score + top-k kernel
+  (or the GEMV kernel for batches of at most 8) and a merge kernel;
+* there is no CPU storage and no fallback: a non-CUDA device or a GPU other than
+  sm_100 raises RuntimeError. ``method="torch"`` (cuBLAS + topk) remains available
+  on request, as in the reference.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import _ext
+from .reference import torch_topk
+
+PAD = 64  # width granularity (reference index.py:14)
+MAX_FUSED_K = 1024  # reference: 256 (index.py:15); larger k runs on the same kernels here
+_INGEST_CHUNK = 1 << 18  # rows staged per host->device copy
+
+METHODS = ("auto", "fused", "twopass", "torch")
+
+_KERNEL_DTYPES = (torch.float32, torch.float16, torch.bfloat16, torch.float64)
+
+
+def _to_tensor(a) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        return a
+    return torch.from_numpy(np.ascontiguousarray(a))
+
+
+def pad_width(d: int) -> int:
+    return -(-int(d) // PAD) * PAD
+
+
+def _ingest(src: torch.Tensor, device: torch.device, cosine: bool, out: torch.Tensor | None = None):
+    """fp16, optionally L2-normalised, width-padded copy of ``src`` on ``device``.
+
+    ``src`` may live on the host (staged through in chunks) or on the device. When
+    ``out`` is ``src`` itself the rows are normalised in place.
+    """
+    mod = _ext.load()
+    if src.dtype not in _KERNEL_DTYPES:
+        src = src.to(torch.float32)
+    n, d = src.shape
+    if out is None:
+        out = torch.empty((n, pad_width(d)), dtype=torch.float16, device=device)
+    if n == 0:
+        return out
+    if src.device == device:
+        if src.stride(1) != 1:
+            src = src.contiguous()
+        mod.ingest_into(src, out, cosine)
+        return out
+    # Host source: stage fixed-size row blocks so a huge array never needs a
+    # second full-size copy on either side.
+    with torch.cuda.device(device):
+        for start in range(0, n, _INGEST_CHUNK):
+            blk = src[start : start + _INGEST_CHUNK]
+            blk_dev = blk.to(device, non_blocking=blk.is_pinned())
+            if blk_dev.stride(1) != 1:
+                blk_dev = blk_dev.contiguous()
+            mod.ingest_into(blk_dev, out[start : start + blk.shape[0]], cosine)
+    return out
+
+
+class Index:
+    """Brute-force (exact) top-k index on one B200.
+
+    Args:
+        embeddings: [n, d] array or tensor (any float dtype; host or device).
+            Stored as fp16 rows zero-padded to a multiple of 64 columns.
+        metric: "cosine" (rows and queries are L2-normalised) or "ip" (raw inner product).
+        device: "cuda", "cuda:1", ...; defaults to the current CUDA device. Only
+            CUDA devices of compute capability 10.0 are supported.
+        copy: if False and ``embeddings`` is already a contiguous fp16 tensor on
+            ``device`` whose width is a multiple of 64, it is used as-is (and
+            normalised in place for cosine).
+    """
+
+    def __init__(self, embeddings, metric: str = "cosine", device=None, copy: bool = True):
+        if metric not in ("cosine", "ip"):
+            raise ValueError("metric must be 'cosine' or 'ip'")
+        x = _to_tensor(embeddings)
+        if x.dim() != 2:
+            raise ValueError("embeddings must be 2-D [n, d]")
+        if x.shape[0] == 0:
+            raise ValueError("embeddings is empty")
+        if device is None:
+            if not torch.cuda.is_available():
+                raise RuntimeError("cuda_vector_search (B200 build) needs a CUDA device; none is available")
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("cuda_vector_search (B200 build) stores the index on a CUDA device only")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        _ext.load()  # raises unless the sm_100 extension is usable
+        self.metric = metric
+        self.dim = int(x.shape[1])
+        if x.shape[0] >= 2**31 - 1:
+            raise ValueError("embeddings must have fewer than 2^31 - 1 rows")
+        cosine = metric == "cosine"
+        in_place = (
+            not copy
+            and x.device == self.device
+            and x.dtype == torch.float16
+            and x.is_contiguous()
+            and self.dim % PAD == 0
+        )
+        self._x = _ingest(x, self.device, cosine, out=x if in_place else None)
+        self._use_kernels = True
+
+    # -- basics -------------------------------------------------------------
+    def __len__(self) -> int:
+        return int(self._x.shape[0])
+
+    @property
+    def embeddings(self) -> torch.Tensor:
+        """The stored matrix (normalised for cosine), without padding."""
+        return self._x[:, : self.dim]
+
+    def _prep_queries(self, queries) -> torch.Tensor:
+        q = _to_tensor(queries)
+        if q.dim() == 1:
+            q = q[None]
+        if q.dim() != 2 or q.shape[1] != self.dim:
+            raise ValueError(f"queries must be [b, {self.dim}]")
+        return _ingest(q, self.device, self.metric == "cosine")
+
+    # -- search -------------------------------------------------------------
+    def search(self, queries, k: int = 10, method: str = "auto"):
+        """Return (scores [b, k] float32, ids [b, k] int64), best first.
+
+        method:
+            "fused"   - tcgen05 (or GEMV for b <= 8) scores + top-k in one pass (k <= 1024)
+            "twopass" - score kernel writes the full matrix, then torch.topk
+            "torch"   - torch.matmul (cuBLAS) + torch.topk
+            "auto"    - fused when k <= 1024, else twopass
+        """
+        if method not in METHODS:
+            raise ValueError(f"method must be one of {METHODS}")
+        k = int(k)
+        if k < 1:
+            raise ValueError("k must be >= 1")
+        k = min(k, len(self))
+        q = self._prep_queries(queries)
+        if method == "auto":
+            method = "fused" if k <= MAX_FUSED_K else "twopass"
+        mod = _ext.load()
+        if method == "fused":
+            if k > MAX_FUSED_K:
+                raise ValueError(f"fused search supports k <= {MAX_FUSED_K}")
+            v, i, _ = mod.fused_topk(q, self._x, k)
+            return v, i
+        if method == "twopass":
+            s = mod.scores(q, self._x, False)
+            v, i = torch.topk(s, k, dim=1)
+            return v.float(), i
+        return torch_topk(q, self._x, k)
+
+    def scores(self, queries, fp32: bool = True) -> torch.Tensor:
+        """Full [b, n] score matrix from the tcgen05 score kernel."""
+        q = self._prep_queries(queries)
+        return _ext.load().scores(q, self._x, fp32)
+
+    # -- persistence --------------------------------------------------------
+    def save(self, path) -> None:
+        """Write the stored vectors to `path` (.npy, fp16) plus a small `<path>.json` sidecar."""
+        path = Path(path)
+        np.save(path, self.embeddings.to(torch.float16).cpu().numpy())
+        meta = {"metric": self.metric, "dim": self.dim, "n": len(self)}
+        Path(str(path) + ".json").write_text(json.dumps(meta))
+
+    @classmethod
+    def load(cls, path, metric: str | None = None, device=None) -> "Index":
+        path = Path(path)
+        if metric is None:
+            side = Path(str(path) + ".json")
+            metric = json.loads(side.read_text())["metric"] if side.exists() else "cosine"
+        x = torch.from_numpy(np.load(path))
+        return cls(x, metric=metric, device=device, copy=False)

@@ -1,0 +1,123 @@
+"""Row-sharded exact search across GPUs: one process per GPU, torch.distributed.
+
+The reference has no multi-GPU path; its chunked ground truth
+(cuda_vector_search/reference.py:22-33: local top-k per chunk, ids shifted by the
+chunk start, concatenate, top-k again) is the template. Here each rank owns a
+contiguous row range of the corpus, runs the fused search on it with its global
+row offset folded into the ids, the ranks all-gather their [b, k] (score, id)
+lists (NCCL over NVLink), and every rank merges the [world, b, k] lists with the
+merge kernel. There is exactly one collective per search and it carries
+12 * b * k bytes per rank.
+
+Ordering is exact and global: score descending, then smaller global id, the same
+rule as the single-GPU index, because every per-rank list is complete for its
+rows and the merge compares (score, global id) keys.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import _ext
+from .index import Index
+
+
+def all_gather_stacked(t: torch.Tensor, group=None) -> torch.Tensor:
+    """[world, *t.shape] gather of ``t`` from every rank (same shape everywhere)."""
+    world = dist.get_world_size(group)
+    out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), t.contiguous(), group=group)
+    return out
+
+
+@dataclass
+class ShardOps:
+    """The per-rank operations a sharded search needs.
+
+    local_topk(queries, k, id_offset) -> (scores [b, k] f32, ids [b, k] i64, sorted
+    best first, ids already global, empty slots id -1); merge(scores [W, b, k],
+    ids [W, b, k], k) -> (scores [b, k], ids [b, k]).
+    """
+
+    local_topk: Callable
+    merge: Callable
+    n_local: int
+    device: torch.device
+
+
+def cuda_shard_ops(index: Index) -> ShardOps:
+    """Operations backed by this package's kernels for one rank's Index."""
+    mod = _ext.load()
+
+    def local_topk(queries, k, id_offset):
+        q = index._prep_queries(queries)
+        b = q.shape[0]
+        kk = min(k, len(index))
+        v = torch.empty((b, kk), dtype=torch.float32, device=index.device)
+        i = torch.empty((b, kk), dtype=torch.int64, device=index.device)
+        ws = torch.empty(max(256, mod.workspace_size(b, len(index), index._x.shape[1], kk)),
+                         dtype=torch.uint8, device=index.device)
+        mod.fused_topk_into(q, index._x, kk, id_offset, v, i, ws)
+        if kk < k:  # shard smaller than k: pad with empty slots
+            v = torch.cat([v, v.new_full((b, k - kk), float("-inf"))], 1)
+            i = torch.cat([i, i.new_full((b, k - kk), -1)], 1)
+        return v, i
+
+    def merge(v_all, i_all, k):
+        return mod.merge_lists(v_all.contiguous(), i_all.contiguous(), k)
+
+    return ShardOps(local_topk=local_topk, merge=merge, n_local=len(index), device=index.device)
+
+
+class ShardedIndex:
+    """Exact top-k over a corpus whose rows are split across the ranks of a group.
+
+    Every rank constructs it collectively with its own contiguous block of rows
+    (rank r holds the rows after those of ranks 0..r-1). ``search`` is also
+    collective: every rank passes the same queries and receives the same
+    (scores [b, k] f32, ids [b, k] i64) with global row ids, best first.
+    """
+
+    def __init__(self, shard_embeddings=None, metric: str = "cosine", device=None, group=None,
+                 copy: bool = True, ops: ShardOps | None = None):
+        if not dist.is_available() or not dist.is_initialized():
+            raise RuntimeError("ShardedIndex needs an initialised torch.distributed process group")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if ops is None:
+            if shard_embeddings is None:
+                raise ValueError("shard_embeddings is required")
+            self.local = Index(shard_embeddings, metric=metric, device=device, copy=copy)
+            ops = cuda_shard_ops(self.local)
+        else:
+            self.local = None
+        self.ops = ops
+        self.metric = metric
+        sizes = all_gather_stacked(torch.tensor([ops.n_local], dtype=torch.int64, device=ops.device), group)
+        sizes = [int(s) for s in sizes.flatten().tolist()]
+        self.shard_sizes = sizes
+        self.row_offset = sum(sizes[: self.rank])
+        self.n_total = sum(sizes)
+        if self.n_total >= 2**31:
+            raise ValueError("a sharded corpus must have fewer than 2^31 rows in total")
+
+    def __len__(self) -> int:
+        return self.n_total
+
+    def search(self, queries, k: int = 10):
+        k = int(k)
+        if k < 1:
+            raise ValueError("k must be >= 1")
+        k = min(k, self.n_total)
+        v, i = self.ops.local_topk(queries, k, self.row_offset)
+        v_all = all_gather_stacked(v, self.group)
+        i_all = all_gather_stacked(i, self.group)
+        return self.ops.merge(v_all, i_all, k)
