@@ -394,3 +394,79 @@ cvs_status cvs_set_profile_events(void* start_event, void* stop_event) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free search entry point.
+//
+// Some callers cannot hand this library a device workspace: a host program that
+// owns the whole device-memory budget through its own pool and does not let
+// plugins call cudaMalloc, a latency-critical serving loop where cudaMalloc's
+// implicit synchronisation is not acceptable, or a foreign-language binding
+// (Go, Java, ...) with no device allocator of its own. cvs_fused_topk_noalloc
+// serves them: it runs the same search kernels as cvs_fused_topk, but their
+// per-segment candidate lists live in the fixed array below instead of a
+// caller-provided workspace.
+//
+// The array is a static __device__ object, so every GPU that loads this library
+// keeps kNoAllocScratchBytes reserved for it until the process exits. Host code
+// cannot use the array's name as a device address; the address is looked up once
+// per device with cudaGetSymbolAddress, on the first call made on that device.
+// That first call therefore does a little set-up work and should be made before
+// any stream capture begins.
+//
+// All calls on a device share the one array. Nothing in it has to start at zero
+// (each call writes every slot its merge step reads), but two calls whose kernels
+// overlap on the GPU -- different streams, or different host threads -- race on
+// it; serialise them on one stream.
+// ---------------------------------------------------------------------------
+namespace cvs {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+std::unordered_map<int, void*> g_noalloc_addr;
+
+// Device address of g_noalloc_scratch on the current device (looked up once).
+cvs_status noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  auto it = g_noalloc_addr.find(dev);
+  if (it == g_noalloc_addr.end()) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    it = g_noalloc_addr.emplace(dev, p).first;
+  }
+  *out = it->second;
+  return CVS_OK;
+}
+
+}  // namespace
+}  // namespace cvs
+
+extern "C" cvs_status cvs_fused_topk_noalloc(const void* q_f16, int64_t b, const void* x_f16,
+                                             int64_t n, int d_pad, int k, int64_t id_offset,
+                                             float* out_scores, int64_t* out_ids, int plan_chunks,
+                                             void* stream) {
+  cvs_status st = check_pair(q_f16, b, x_f16, n, d_pad);
+  if (st != CVS_OK) return st;
+  if (b == 0) return CVS_OK;
+  DeviceInfo dev;
+  if ((st = device_info(&dev)) != CVS_OK) return st;
+  Plan p;
+  if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p)) != CVS_OK) return st;
+  if (p.ws_bytes > kNoAllocScratchBytes)
+    return fail(CVS_ERR_WORKSPACE,
+                "this search needs %zu bytes of scratch but the built-in scratch holds %zu "
+                "(b * segments * list slots * 8 bytes); use fewer queries per call, a smaller k "
+                "or fewer chunks, or call cvs_fused_topk with a workspace",
+                p.ws_bytes, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if ((st = noalloc_scratch(&scratch)) != CVS_OK) return st;
+  return cvs_fused_topk(q_f16, b, x_f16, n, d_pad, k, id_offset, out_scores, out_ids, scratch,
+                        kNoAllocScratchBytes, 0, plan_chunks, nullptr, stream);
+}

@@ -105,6 +105,23 @@ cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t list
                            int64_t len, int k, float* out_scores, int64_t* out_ids, void* stream);
 
 /*
+ * Same search as cvs_fused_topk, for callers that cannot allocate device
+ * memory (a host application that owns the device-memory budget and forbids
+ * plugins from calling cudaMalloc, a serving loop that cannot afford
+ * cudaMalloc's synchronisation, a language binding without a device
+ * allocator). The candidate lists live in a 16 MiB array built into the
+ * library (reserved on every GPU that loads it until the process exits); a
+ * problem needing more (b * segments * list slots * 8 bytes, as reported by
+ * cvs_fused_topk_workspace_size) is rejected with CVS_ERR_WORKSPACE. The first
+ * call on a device looks up the array's address (make it before any stream
+ * capture). All calls share the array: calls that overlap on the GPU race, so
+ * issue them on one stream. Allocates nothing. No counterpart in the reference.
+ */
+cvs_status cvs_fused_topk_noalloc(const void* q_f16, int64_t b, const void* x_f16, int64_t n,
+                                  int d_pad, int k, int64_t id_offset, float* out_scores,
+                                  int64_t* out_ids, int plan_chunks, void* stream);
+
+/*
  * Reads and clears the device error word of `device` (synchronous). *code is 0
  * when no kernel reported an error since the last poll; otherwise the status is
  * CVS_ERR_DEVICE_TIMEOUT and *code says which wait gave up. No reference
