@@ -377,8 +377,14 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0, help="override rows per GPU (profiling runs)")
+    ap.add_argument("--batch", type=int, default=0, help="override the batch size (profiling runs)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.rows:
+        cfg["n"] = args.rows
+    if args.batch:
+        cfg["b"] = args.batch
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -129,6 +129,8 @@ struct Plan {
   bool qres = false;
   int qtiles = 0, segs = 0, tiles_per_seg = 0, ntiles = 0;
   int cap = 0;
+  int lists = 0;  // candidate lists per query (segments x lists per segment)
+  size_t bound_bytes = 0;  // per-query shared bounds at the start of the workspace
   int rows_per_seg = 0;
   size_t ws_bytes = 0;
 };
@@ -160,7 +162,9 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->rows_per_seg = static_cast<int>((n + segs - 1) / segs);
     p->segs = static_cast<int>((n + p->rows_per_seg - 1) / p->rows_per_seg);
     p->cap = k;
-    p->ws_bytes = round_up(static_cast<size_t>(b) * p->segs * p->cap * 8, kWsAlign);
+    p->lists = p->segs;
+    p->bound_bytes = 0;
+    p->ws_bytes = round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
     return CVS_OK;
   }
   p->gemv = false;
@@ -176,7 +180,9 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->cap = static_cast<int>(round_up(static_cast<size_t>(std::max(2 * k, k + 32)), 32));
   }
   p->qres = (d_pad / kTcK) <= kTcMaxResidentSlices;
-  p->ws_bytes = round_up(static_cast<size_t>(b) * p->segs * p->cap * 8, kWsAlign);
+  p->lists = p->segs * tc_lists_per_segment(p->epi);
+  p->bound_bytes = round_up(static_cast<size_t>(b) * 4, kWsAlign);
+  p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
   return CVS_OK;
 }
 
@@ -253,9 +259,13 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     return fail(CVS_ERR_WORKSPACE, "workspace of %zu bytes (256-byte aligned) required, got %zu at %p",
                 p.ws_bytes, workspace_bytes, workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint64_t* part = static_cast<uint64_t*>(workspace);
+  uint32_t* bounds = static_cast<uint32_t*>(workspace);
+  uint64_t* part = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + p.bound_bytes);
   const bool prof = g_prof_start && g_prof_stop;
   cudaError_t e;
+  // The shared per-query bounds must start at "none" (0) on every call.
+  if (p.bound_bytes && (e = cudaMemsetAsync(bounds, 0, static_cast<size_t>(b) * 4, s)) != cudaSuccess)
+    return cuda_fail(e, "clearing the per-query bounds");
   if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   if (p.gemv) {
     GemvArgs a{};
@@ -286,6 +296,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     a.k = k;
     a.cap = p.cap;
     a.part = part;
+    a.gthr = bounds;
     a.err = dev.err;
     if ((e = tc_launch(p.epi, p.qres, &qmap, &xmap, a, s)) != cudaSuccess)
       return cuda_fail(e, "tcgen05 search launch");
@@ -294,7 +305,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   MergeKeysArgs m{};
   m.part = part;
   m.b = static_cast<int>(b);
-  m.lists = p.segs;
+  m.lists = p.lists;
   m.stride = p.cap;
   m.per_list = k;
   m.k = k;
@@ -414,10 +425,11 @@ cvs_status cvs_set_profile_events(void* start_event, void* stop_event) {
 // That first call therefore does a little set-up work and should be made before
 // any stream capture begins.
 //
-// All calls on a device share the one array. Nothing in it has to start at zero
-// (each call writes every slot its merge step reads), but two calls whose kernels
-// overlap on the GPU -- different streams, or different host threads -- race on
-// it; serialise them on one stream.
+// All calls on a device share the one array. The only part that has to start at
+// zero, the per-query bound words at its front, is cleared by every call before
+// its kernels run; every candidate slot the merge reads is written first. Two
+// calls whose kernels overlap on the GPU -- different streams, or different
+// host threads -- race on the array; serialise them on one stream.
 // ---------------------------------------------------------------------------
 namespace cvs {
 namespace {

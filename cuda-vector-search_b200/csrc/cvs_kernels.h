@@ -15,7 +15,6 @@ namespace cvs {
 constexpr int kTcM = 128;          // queries per tile (MMA M; TMEM lanes)
 constexpr int kTcN = 256;          // corpus rows per tile (MMA N; TMEM columns)
 constexpr int kTcK = 64;           // halves per K slice (one 128-byte swizzled row)
-constexpr int kTcThreads = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kTcStages = 4;
 constexpr int kTcMaxResidentSlices = 7;  // queries stay in smem when d_pad <= 448
 
@@ -37,13 +36,16 @@ struct TcArgs {
   int tiles_per_seg;
   int ntiles;         // ceil(n / 256)
   int k;              // candidates kept per (query, segment)
-  int cap;            // slots per (query, segment) list; cap >= k
-  uint64_t* part;     // [b][segs][cap] ordered keys
+  int cap;            // slots per candidate list; cap >= k
+  uint64_t* part;     // [b][segs * lists per segment][cap] ordered keys
+  uint32_t* gthr;     // [b] shared per-query lower bounds (ordered bits), zeroed per call
   void* scores_out;   // [b][n] fp32/fp16 for the store epilogues
   int* err;           // device error word
 };
 
-size_t tc_smem_bytes(bool resident_queries, int ksl);
+// Candidate lists each (query, segment) produces with this epilogue (one per
+// epilogue column stripe); the workspace holds b * segs * lists * cap keys.
+int tc_lists_per_segment(int epi);
 cudaError_t tc_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                       const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
 

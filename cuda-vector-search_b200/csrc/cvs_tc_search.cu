@@ -31,7 +31,10 @@ namespace {
 constexpr int kQSliceBytes = kTcM * kTcK * 2;  // 16 KB
 constexpr int kXSliceBytes = kTcN * kTcK * 2;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr int kEpiWarps = 4;
+// Epilogue warps: kSubs per TMEM lane quadrant (each epilogue type chooses
+// kSubs). Warp 2+e drains quadrant (2+e)%4, column stripe e/4 of every tile.
+__host__ __device__ constexpr int epi_warps(int subs) { return 4 * subs; }
+__host__ __device__ constexpr int tc_threads(int subs) { return 64 + 32 * epi_warps(subs); }
 
 // Resident queries leave room for 3 corpus stages (96 KB in flight, enough to
 // cover HBM latency); streamed queries use 4 stages of 48 KB.
@@ -47,7 +50,7 @@ struct Layout {
   int total;
 };
 
-__host__ __device__ constexpr Layout make_layout(bool qres, int ksl) {
+__host__ __device__ constexpr Layout make_layout(bool qres, int ksl, int subs) {
   Layout l{};
   l.q_res = 0;
   l.stage_bytes = qres ? kXSliceBytes : (kXSliceBytes + kQSliceBytes);
@@ -55,7 +58,7 @@ __host__ __device__ constexpr Layout make_layout(bool qres, int ksl) {
   l.bars = l.stages + num_stages(qres) * l.stage_bytes;
   // full[4], empty[4], tfull[2], tempty[2], qfull, done, tmem holder, abort
   l.hist = l.bars + 8 * (2 * kTcStages + 6) + 16;
-  l.total = l.hist + kEpiWarps * 256 * 4;
+  l.total = l.hist + epi_warps(subs) * 256 * 4;
   return l;
 }
 
@@ -99,28 +102,71 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 // query (rows row0 .. row0+31, of which the first `nvalid` exist).
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ bool any_above(const uint32_t (&r)[32], float thr) {
-  bool any = false;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) any |= __uint_as_float(r[j]) > thr;
-  return any;
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
-// Bit j set when score j exceeds thr (only the first nvalid scores count).
-__device__ __forceinline__ uint32_t above_mask(const uint32_t (&r)[32], float thr, int nvalid) {
-  uint32_t m = 0;
+// Largest of the 32 scores: 17 three-input maxima in a depth-4 tree, so the
+// per-chunk fast reject costs about half an instruction per score.
+__device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
+  float m[11];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) m |= (__uint_as_float(r[j]) > thr ? 1u : 0u) << j;
-  return nvalid >= 32 ? m : (m & ((1u << nvalid) - 1u));
+  for (int i = 0; i < 10; ++i)
+    m[i] = fmax3(__uint_as_float(r[3 * i]), __uint_as_float(r[3 * i + 1]), __uint_as_float(r[3 * i + 2]));
+  m[10] = fmaxf(__uint_as_float(r[30]), __uint_as_float(r[31]));
+  const float a = fmax3(m[0], m[1], m[2]);
+  const float b = fmax3(m[3], m[4], m[5]);
+  const float c = fmax3(m[6], m[7], m[8]);
+  return fmaxf(fmax3(a, b, c), fmaxf(m[9], m[10]));
+}
+
+// Shared per-query lower bound: the largest k-th-best score any list of this
+// query has reached (ordered bits, 0 = none yet). Every list of the query --
+// other column stripes of this CTA and other corpus segments -- holds k
+// candidates at or above it, so the query's final k-th best is at least this
+// high and a score strictly below it can be dropped by every list.
+__device__ __forceinline__ float load_bound(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v ? score_of_bits(v) : -INFINITY;
+}
+
+__device__ __forceinline__ void publish_bound(uint32_t* p, float kth, uint32_t& published) {
+  if (kth == -INFINITY) return;
+  const uint32_t o = ordered_bits(kth);
+  if (o > published) {
+    atomicMax(p, o);
+    published = o;
+  }
+}
+
+// Bit j set when score j exceeds thr and is not below the shared bound (only
+// the first nvalid scores count). Four independent OR chains.
+__device__ __forceinline__ uint32_t above_mask(const uint32_t (&r)[32], float thr, float bound,
+                                               int nvalid) {
+  uint32_t m[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float s = __uint_as_float(r[j]);
+    m[j & 3] |= ((s > thr) && (s >= bound) ? 1u : 0u) << j;
+  }
+  const uint32_t all = (m[0] | m[1]) | (m[2] | m[3]);
+  return nvalid >= 32 ? all : (all & ((1u << nvalid) - 1u));
 }
 
 // r[j] for a run-time j without indexing the register array (which would move
-// it to local memory).
+// it to local memory): a 5-level select tree on the bits of j.
 __device__ __forceinline__ float pick(const uint32_t (&r)[32], int j) {
-  uint32_t v = r[0];
+  uint32_t l[16];
 #pragma unroll
-  for (int t = 1; t < 32; ++t) v = (t == j) ? r[t] : v;
-  return __uint_as_float(v);
+  for (int i = 0; i < 16; ++i) l[i] = (j & 1) ? r[2 * i + 1] : r[2 * i];
+#pragma unroll
+  for (int w = 8, bit = 2; w >= 1; w >>= 1, bit <<= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) l[i] = (j & bit) ? l[2 * i + 1] : l[2 * i];
+  return __uint_as_float(l[0]);
 }
 
 // Sorted (score desc, row asc) list of KP slots in registers holding the best
@@ -129,13 +175,20 @@ __device__ __forceinline__ float pick(const uint32_t (&r)[32], int j) {
 // last slot (a run-time slot index would push the list to local memory).
 template <int KP>
 struct EpiTopkReg {
+  // Four column stripes per quadrant for short lists (16 epilogue warps, 576
+  // threads); two for 32-slot lists, whose registers would not fit four.
+  static constexpr int kSubs = 2;
   float tv[KP];
   uint32_t ti[KP];
-  float thr;
+  float thr;         // this list's k-th best (its last slot)
+  float bound;       // shared lower bound of the query (refreshed per tile)
+  uint32_t published;
   int k;
 
   __device__ __forceinline__ void init(const TcArgs& a) {
     k = a.k;
+    bound = -INFINITY;
+    published = 0;
 #pragma unroll
     for (int j = 0; j < KP; ++j) {
       tv[j] = (j < KP - k) ? INFINITY : -INFINITY;
@@ -144,26 +197,29 @@ struct EpiTopkReg {
     thr = -INFINITY;
   }
 
+  // The list is sorted, so "candidate ranks before slot j" is false for the
+  // leading slots and true from the insertion point on. All KP tests are
+  // independent and the shift is one select per slot: no serial chain.
   __device__ __forceinline__ void insert(float s, uint32_t row) {
-    float cs = s;
-    uint32_t ci = row;
+    bool gt[KP];
 #pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      const bool sw = (cs > tv[j]) || (cs == tv[j] && ci < ti[j]);
-      const float ov = tv[j];
-      const uint32_t oi = ti[j];
-      tv[j] = sw ? cs : ov;
-      ti[j] = sw ? ci : oi;
-      cs = sw ? ov : cs;
-      ci = sw ? oi : ci;
+    for (int j = 0; j < KP; ++j) gt[j] = (s > tv[j]) || (s == tv[j] && row < ti[j]);
+#pragma unroll
+    for (int j = KP - 1; j > 0; --j) {
+      tv[j] = gt[j] ? (gt[j - 1] ? tv[j - 1] : s) : tv[j];
+      ti[j] = gt[j] ? (gt[j - 1] ? ti[j - 1] : row) : ti[j];
     }
+    tv[0] = gt[0] ? s : tv[0];
+    ti[0] = gt[0] ? row : ti[0];
     thr = tv[KP - 1];
   }
 
   __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
                                           bool qvalid, const Shared&, int) {
-    if (!qvalid || !any_above(r, thr)) return;
-    uint32_t m = above_mask(r, thr, nvalid);
+    if (!qvalid) return;
+    const float mx = max32(r);
+    if (!(mx > thr && mx >= bound)) return;
+    uint32_t m = above_mask(r, thr, bound, nvalid);
     while (m) {
       const int j = __ffs(m) - 1;
       m &= m - 1;
@@ -172,9 +228,9 @@ struct EpiTopkReg {
     }
   }
 
-  __device__ __forceinline__ void finish(const TcArgs& a, int q, int seg, bool qvalid, const Shared&, int) {
+  __device__ __forceinline__ void finish(const TcArgs& a, int q, int list, bool qvalid, const Shared&, int) {
     if (!qvalid) return;
-    uint64_t* out = a.part + (static_cast<size_t>(q) * a.segs + seg) * a.cap;
+    uint64_t* out = a.part + (static_cast<size_t>(q) * a.segs * kSubs + list) * a.cap;
 #pragma unroll
     for (int j = 0; j < KP; ++j) {
       if (j >= KP - k) out[j - (KP - k)] = (tv[j] == -INFINITY) ? 0ull : make_key(tv[j], ti[j]);
@@ -186,14 +242,19 @@ struct EpiTopkReg {
 // A key is appended when its score beats the current k-th best; when a list
 // could overflow on the next chunk, the warp cooperatively keeps its top k.
 struct EpiTopkBuf {
+  static constexpr int kSubs = 1;
   uint64_t* list;
   int cnt;
-  float thr;
+  float thr;        // k-th best at the last compaction
+  float bound;      // shared lower bound of the query (refreshed per tile)
+  uint32_t published;
 
   __device__ __forceinline__ void init(const TcArgs&) {
     list = nullptr;
     cnt = 0;
     thr = -INFINITY;
+    bound = -INFINITY;
+    published = 0;
   }
 
   __device__ __forceinline__ void compact_lanes(unsigned need, const TcArgs& a, const Shared& sh,
@@ -209,14 +270,16 @@ struct EpiTopkBuf {
         cnt = a.k;
         thr = key_score(kth);
       }
+      (void)sh;
     }
   }
 
   __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
                                           bool qvalid, const Shared& sh, int ew) {
     // `list` is set lazily so the pointer math stays out of the hot loop.
-    if (qvalid && any_above(r, thr)) {
-      uint32_t m = above_mask(r, thr, nvalid);
+    const float mx = max32(r);
+    if (qvalid && mx > thr && mx >= bound) {
+      uint32_t m = above_mask(r, thr, bound, nvalid);
       while (m) {
         const int j = __ffs(m) - 1;
         m &= m - 1;
@@ -239,6 +302,7 @@ struct EpiTopkBuf {
 // Writes the score tile to [b][n] (fp32 or fp16).
 template <bool F32>
 struct EpiStore {
+  static constexpr int kSubs = 2;
   __device__ __forceinline__ void init(const TcArgs&) {}
   __device__ __forceinline__ void consume_store(const uint32_t (&r)[32], int row0, int nvalid,
                                                 bool qvalid, const TcArgs& a, int q) {
@@ -288,7 +352,7 @@ struct is_store<EpiStore<F>> : std::true_type {};
 // The kernel
 // ---------------------------------------------------------------------------
 template <bool QRES, class Epi>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     tc_search_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap xmap, const TcArgs a) {
   constexpr int kS = num_stages(QRES);  // ring depth (barrier arrays are sized for the max)
@@ -296,7 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   Shared sh;
   sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
-  sh.l = make_layout(QRES, a.ksl);
+  sh.l = make_layout(QRES, a.ksl, Epi::kSubs);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -314,7 +378,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(sh.tfull(t), 1);
-      mbar_init(sh.tempty(t), kEpiWarps);
+      mbar_init(sh.tempty(t), epi_warps(Epi::kSubs));
     }
     mbar_init(sh.qfull(), 1);
     mbar_init(sh.done(), 1);
@@ -413,7 +477,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------ epilogue ----------------------------------
-    const int ew = warp - 2;             // 0..3
+    constexpr int kChunks = kTcN / 32 / Epi::kSubs;  // 32-column chunks per warp per tile
+    const int ew = warp - 2;             // 0 .. 4*kSubs-1
+    const int sub = ew >> 2;             // column stripe
     const int quad = warp & 3;           // TMEM lane quadrant this warp may access
     const int q = qt * kTcM + quad * 32 + lane;
     const bool qvalid = q < a.b;
@@ -421,20 +487,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     Epi epi;
     epi.init(a);
     if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
-      if (qvalid) epi.list = a.part + (static_cast<size_t>(q) * a.segs + seg) * a.cap;
+      if (qvalid) epi.list = a.part + (static_cast<size_t>(q) * a.segs + seg) * a.cap;  // kSubs == 1
     }
     bool ok = true;
     for (int t = 0; t < ntl; ++t) {
       const int acc = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
+      float fresh = -INFINITY;
+      if constexpr (!is_store<Epi>::value) {
+        if (qvalid) fresh = load_bound(a.gthr + q);  // overlaps the wait below
+      }
       if (!mbar_wait(sh.tfull(acc), use & 1, abort, a.err, 5)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if constexpr (!is_store<Epi>::value) epi.bound = fmaxf(epi.bound, fresh);
       const int row0 = (t_begin + t) * kTcN;
       const int valid = min(kTcN, a.n - row0);
-      for (int c = 0; c < kTcN / 32; ++c) {
+      for (int c = sub * kChunks; c < (sub + 1) * kChunks; ++c) {
         if (c * 32 >= valid) break;
         uint32_t r[32];
         tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(acc * kTcN + c * 32), r);
@@ -453,9 +524,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sh.tempty(acc));
+      if constexpr (!is_store<Epi>::value) {
+        if (qvalid) publish_bound(a.gthr + q, epi.thr, epi.published);
+      }
     }
     if constexpr (!is_store<Epi>::value) {
-      if (ok) epi.finish(a, q, seg, qvalid, sh, ew);
+      if (ok) epi.finish(a, q, seg * Epi::kSubs + sub, qvalid, sh, ew);
     }
   }
 
@@ -470,14 +544,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 template <bool QRES, class Epi>
 cudaError_t launch_one(const CUtensorMap* qmap, const CUtensorMap* xmap, const TcArgs& a,
                        cudaStream_t stream) {
-  const Layout l = make_layout(QRES, a.ksl);
+  const Layout l = make_layout(QRES, a.ksl, Epi::kSubs);
   const size_t smem = static_cast<size_t>(l.total) + 1024;
   auto kern = tc_search_kernel<QRES, Epi>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const unsigned grid = static_cast<unsigned>(a.qtiles) * static_cast<unsigned>(a.segs);
-  kern<<<grid, kTcThreads, smem, stream>>>(*qmap, *xmap, a);
+  kern<<<grid, tc_threads(Epi::kSubs), smem, stream>>>(*qmap, *xmap, a);
   return cudaGetLastError();
 }
 
@@ -496,8 +570,13 @@ cudaError_t launch_epi(int epi, const CUtensorMap* qmap, const CUtensorMap* xmap
 
 }  // namespace
 
-size_t tc_smem_bytes(bool resident_queries, int ksl) {
-  return static_cast<size_t>(make_layout(resident_queries, ksl).total) + 1024;
+int tc_lists_per_segment(int epi) {
+  switch (epi) {
+    case kEpiTopkReg16: return EpiTopkReg<16>::kSubs;
+    case kEpiTopkReg32: return EpiTopkReg<32>::kSubs;
+    case kEpiTopkBuf: return EpiTopkBuf::kSubs;
+    default: return 1;
+  }
 }
 
 cudaError_t tc_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
