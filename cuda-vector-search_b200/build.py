@@ -30,7 +30,7 @@ INCLUDE = REPO / "include"
 BUILD = HERE / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["cvs_tc_search.cu", "cvs_gemv.cu", "cvs_merge.cu", "cvs_ingest.cu", "cvs_capi.cu"]
+CU_SOURCES = ["cvs_tc_search.cu", "cvs_tc_pair.cu", "cvs_gemv.cu", "cvs_merge.cu", "cvs_ingest.cu", "cvs_capi.cu"]
 LIB_NAME = "libcvs_b200.so"
 
 

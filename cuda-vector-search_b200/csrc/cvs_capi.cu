@@ -125,6 +125,7 @@ cvs_status check_pair(const void* q, int64_t b, const void* x, int64_t n, int d_
 
 struct Plan {
   bool gemv = false;
+  bool pair = false;  // CTA-pair tcgen05 kernel (batches > 128)
   int epi = 0;
   bool qres = false;
   int qtiles = 0, segs = 0, tiles_per_seg = 0, ntiles = 0;
@@ -139,18 +140,49 @@ constexpr size_t kWsAlign = 256;
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Corpus segmentation for the tcgen05 kernel: about one CTA per SM in total.
-void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks) {
-  p->qtiles = static_cast<int>((b + kTcM - 1) / kTcM);
+// Clusters of the pair kernel that can be resident at once (cached: it is a
+// property of the kernel, its shared memory and the device).
+int pair_clusters(int epi, bool qres, int ksl, int sms) {
+  static std::mutex mu;
+  static std::unordered_map<long long, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long long key = (static_cast<long long>(dev) << 32) | (epi << 16) | (qres ? 1 << 8 : 0) | ksl;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = tc_pair_max_clusters(epi, qres, ksl);
+  if (n <= 0) n = sms / 2;
+  cache.emplace(key, n);
+  return n;
+}
+
+// Corpus segmentation for the tcgen05 kernels: one CTA (or CTA pair) per SM
+// (pair) in total. Batches of more than 128 queries use the pair kernel, whose
+// query tiles hold 256 queries.
+void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks, int epi, int d_pad, int bq = 0) {
+  const int ksl = d_pad / kTcK;
+  // bq hint: 16..128 keeps 128-query tiles on one CTA, 256 asks for CTA pairs.
+  p->pair = bq > 0 ? (bq > kTcM && b > kTcM) : (b > kTcM);
   p->ntiles = static_cast<int>((n + kTcN - 1) / kTcN);
-  int segs = chunks > 0 ? chunks : std::max(1, sms / std::max(1, p->qtiles));
+  int slots;
+  if (p->pair) {
+    p->qtiles = static_cast<int>((b + 2 * kTcM - 1) / (2 * kTcM));
+    p->qres = tc_pair_resident_queries(ksl);
+    slots = pair_clusters(epi, p->qres, ksl, sms);
+  } else {
+    p->qtiles = static_cast<int>((b + kTcM - 1) / kTcM);
+    p->qres = ksl <= kTcMaxResidentSlices;
+    slots = sms;
+  }
+  int segs = chunks > 0 ? chunks : std::max(1, slots / std::max(1, p->qtiles));
   segs = std::max(1, std::min(segs, p->ntiles));
   p->tiles_per_seg = (p->ntiles + segs - 1) / segs;
   p->segs = (p->ntiles + p->tiles_per_seg - 1) / p->tiles_per_seg;
 }
 
 cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const DeviceInfo& dev,
-                      Plan* p) {
+                      Plan* p, int bq = 0) {
   if (k < 1 || k > CVS_MAX_FUSED_K)
     return fail(CVS_ERR_INVALID_ARGUMENT, "fused top-k supports 1 <= k <= %d (got %d)", CVS_MAX_FUSED_K, k);
   if (k > n) return fail(CVS_ERR_INVALID_ARGUMENT, "k (%d) must not exceed the corpus size (%lld)", k, (long long)n);
@@ -168,7 +200,6 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     return CVS_OK;
   }
   p->gemv = false;
-  plan_tc_grid(p, b, n, dev.sms, chunks);
   if (k <= 16) {
     p->epi = kEpiTopkReg16;
     p->cap = k;
@@ -179,9 +210,10 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->epi = kEpiTopkBuf;
     p->cap = static_cast<int>(round_up(static_cast<size_t>(std::max(2 * k, k + 32)), 32));
   }
-  p->qres = (d_pad / kTcK) <= kTcMaxResidentSlices;
+  plan_tc_grid(p, b, n, dev.sms, chunks, p->epi, d_pad, bq);
   p->lists = p->segs * tc_lists_per_segment(p->epi);
-  p->bound_bytes = round_up(static_cast<size_t>(b) * 4, kWsAlign);
+  // Per-query shared bound and per-list best scores, both cleared per call.
+  p->bound_bytes = round_up(static_cast<size_t>(b) * 4 * (1 + p->lists), kWsAlign);
   p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
   return CVS_OK;
 }
@@ -233,7 +265,7 @@ cvs_status cvs_fused_topk_workspace_size(int64_t b, int64_t n, int d_pad, int k,
   cvs_status st = device_info(&dev);
   if (st != CVS_OK) return st;
   Plan p;
-  st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p);
+  st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p, plan_bq);
   if (st != CVS_OK) return st;
   *bytes = p.ws_bytes;
   return CVS_OK;
@@ -248,9 +280,9 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   DeviceInfo dev;
   if ((st = device_info(&dev)) != CVS_OK) return st;
   Plan p;
-  if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p)) != CVS_OK) return st;
+  if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p, plan_bq)) != CVS_OK) return st;
   if (plan_out) {
-    plan_out[0] = plan_bq > 0 ? plan_bq : (p.gemv ? static_cast<int64_t>(b) : static_cast<int64_t>(kTcM));
+    plan_out[0] = plan_bq > 0 ? plan_bq : (p.gemv ? static_cast<int64_t>(b) : static_cast<int64_t>(p.pair ? 2 * kTcM : kTcM));
     plan_out[1] = p.segs;
   }
   if (b == 0) return CVS_OK;
@@ -264,7 +296,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   const bool prof = g_prof_start && g_prof_stop;
   cudaError_t e;
   // The shared per-query bounds must start at "none" (0) on every call.
-  if (p.bound_bytes && (e = cudaMemsetAsync(bounds, 0, static_cast<size_t>(b) * 4, s)) != cudaSuccess)
+  if (p.bound_bytes && (e = cudaMemsetAsync(bounds, 0, static_cast<size_t>(b) * 4 * (1 + p.lists), s)) != cudaSuccess)
     return cuda_fail(e, "clearing the per-query bounds");
   if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   if (p.gemv) {
@@ -283,7 +315,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   } else {
     CUtensorMap qmap, xmap;
     if ((st = make_map(&qmap, q_f16, b, d_pad, kTcM)) != CVS_OK) return st;
-    if ((st = make_map(&xmap, x_f16, n, d_pad, kTcN)) != CVS_OK) return st;
+    if ((st = make_map(&xmap, x_f16, n, d_pad, p.pair ? kTcN / 2 : kTcN)) != CVS_OK) return st;
     TcArgs a{};
     a.b = static_cast<int>(b);
     a.n = static_cast<int>(n);
@@ -297,9 +329,10 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     a.cap = p.cap;
     a.part = part;
     a.gthr = bounds;
+    a.tops = bounds + b;
     a.err = dev.err;
-    if ((e = tc_launch(p.epi, p.qres, &qmap, &xmap, a, s)) != cudaSuccess)
-      return cuda_fail(e, "tcgen05 search launch");
+    e = p.pair ? tc_pair_launch(p.epi, p.qres, &qmap, &xmap, a, s) : tc_launch(p.epi, p.qres, &qmap, &xmap, a, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 search launch");
   }
   if (prof && (e = cudaEventRecord(g_prof_stop, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   MergeKeysArgs m{};
@@ -326,10 +359,11 @@ cvs_status cvs_scores(const void* q_f16, int64_t b, const void* x_f16, int64_t n
   DeviceInfo dev;
   if ((st = device_info(&dev)) != CVS_OK) return st;
   Plan p;
-  plan_tc_grid(&p, b, n, dev.sms, 0);
+  const int epi = out_fp32 ? kEpiStoreF32 : kEpiStoreF16;
+  plan_tc_grid(&p, b, n, dev.sms, 0, epi, d_pad);
   CUtensorMap qmap, xmap;
   if ((st = make_map(&qmap, q_f16, b, d_pad, kTcM)) != CVS_OK) return st;
-  if ((st = make_map(&xmap, x_f16, n, d_pad, kTcN)) != CVS_OK) return st;
+  if ((st = make_map(&xmap, x_f16, n, d_pad, p.pair ? kTcN / 2 : kTcN)) != CVS_OK) return st;
   TcArgs a{};
   a.b = static_cast<int>(b);
   a.n = static_cast<int>(n);
@@ -343,9 +377,8 @@ cvs_status cvs_scores(const void* q_f16, int64_t b, const void* x_f16, int64_t n
   a.cap = 1;
   a.scores_out = out;
   a.err = dev.err;
-  const bool qres = (d_pad / kTcK) <= kTcMaxResidentSlices;
-  cudaError_t e = tc_launch(out_fp32 ? kEpiStoreF32 : kEpiStoreF16, qres, &qmap, &xmap, a,
-                            static_cast<cudaStream_t>(stream));
+  cudaError_t e = p.pair ? tc_pair_launch(epi, p.qres, &qmap, &xmap, a, static_cast<cudaStream_t>(stream))
+                         : tc_launch(epi, p.qres, &qmap, &xmap, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 score launch");
   return CVS_OK;
 }

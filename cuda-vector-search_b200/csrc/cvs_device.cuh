@@ -82,6 +82,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait that ignores the abort flag; used only to drain work that was
+// already issued before leaving on an error path.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tiled tensor copies global -> shared, completion on an mbarrier)
 // ---------------------------------------------------------------------------
@@ -109,6 +118,19 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, ui
       "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// 2-D tile load into this CTA's shared memory whose completion is counted on an
+// mbarrier of the even CTA of a tcgen05 CTA pair (bar_cluster: a shared::cluster
+// address obtained with map_to_rank). No multicast: one destination CTA.
+__device__ __forceinline__ void tma_load_2d_to_pair_bar(void* smem_dst, const void* desc,
+                                                        uint32_t bar_cluster, int x, int y,
+                                                        uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
 
@@ -198,6 +220,75 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
          | (0u << 7) | (0u << 10)                     // A, B: f16
          | (static_cast<uint32_t>(n >> 3) << 17)      // N >> 3
          | (static_cast<uint32_t>(m >> 4) << 24);     // M >> 4
+}
+
+// ---------------------------------------------------------------------------
+// Clusters and CTA pairs (tcgen05 cta_group::2)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs of the cluster arrives and waits.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared::cluster address of the same shared variable in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Pair MMA, issued by one thread of the even CTA: A rows 0-127 and B rows
+// 0..N/2-1 come from this CTA's shared memory, A rows 128-255 and the other
+// half of B from the odd CTA's shared memory at the same offsets; each CTA's
+// TMEM receives its 128 rows of D.
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier at this offset in every CTA of cta_mask when all
+// pair MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t elect_one_lane() {

@@ -39,6 +39,7 @@ struct TcArgs {
   int cap;            // slots per candidate list; cap >= k
   uint64_t* part;     // [b][segs * lists per segment][cap] ordered keys
   uint32_t* gthr;     // [b] shared per-query lower bounds (ordered bits), zeroed per call
+  uint32_t* tops;     // [b][segs * lists per segment] each list's best score (ordered bits), zeroed per call
   void* scores_out;   // [b][n] fp32/fp16 for the store epilogues
   int* err;           // device error word
 };
@@ -48,6 +49,13 @@ struct TcArgs {
 int tc_lists_per_segment(int epi);
 cudaError_t tc_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                       const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
+
+// CTA-pair variant (batches > 128): a.qtiles counts 256-query pair tiles, the
+// corpus tensor map uses 128-row boxes, the grid is 2 * qtiles * segs CTAs.
+bool tc_pair_resident_queries(int ksl);
+int tc_pair_max_clusters(int epi, bool resident_queries, int ksl);
+cudaError_t tc_pair_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
+                           const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
 
 // ---- CUDA-core GEMV + top-k for batches of at most 8 queries ---------------
 constexpr int kGemvThreads = 256;

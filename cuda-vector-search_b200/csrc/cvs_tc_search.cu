@@ -21,6 +21,7 @@
 #include <type_traits>
 
 #include "cvs_device.cuh"
+#include "cvs_epilogue.cuh"
 #include "cvs_kernels.h"
 #include "cvs_select.cuh"
 
@@ -87,266 +88,6 @@ struct Shared {
     return reinterpret_cast<uint32_t*>(base + l.hist) + 256 * w;
   }
 };
-
-// Bounded wait that ignores the abort flag; used only to drain work that was
-// already issued before leaving on an error path.
-__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Epilogues. consume() sees 32 consecutive corpus scores of this thread's
-// query (rows row0 .. row0+31, of which the first `nvalid` exist).
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
-// Largest of the 32 scores: 17 three-input maxima in a depth-4 tree, so the
-// per-chunk fast reject costs about half an instruction per score.
-__device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
-  float m[11];
-#pragma unroll
-  for (int i = 0; i < 10; ++i)
-    m[i] = fmax3(__uint_as_float(r[3 * i]), __uint_as_float(r[3 * i + 1]), __uint_as_float(r[3 * i + 2]));
-  m[10] = fmaxf(__uint_as_float(r[30]), __uint_as_float(r[31]));
-  const float a = fmax3(m[0], m[1], m[2]);
-  const float b = fmax3(m[3], m[4], m[5]);
-  const float c = fmax3(m[6], m[7], m[8]);
-  return fmaxf(fmax3(a, b, c), fmaxf(m[9], m[10]));
-}
-
-// Shared per-query lower bound: the largest k-th-best score any list of this
-// query has reached (ordered bits, 0 = none yet). Every list of the query --
-// other column stripes of this CTA and other corpus segments -- holds k
-// candidates at or above it, so the query's final k-th best is at least this
-// high and a score strictly below it can be dropped by every list.
-__device__ __forceinline__ float load_bound(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v ? score_of_bits(v) : -INFINITY;
-}
-
-__device__ __forceinline__ void publish_bound(uint32_t* p, float kth, uint32_t& published) {
-  if (kth == -INFINITY) return;
-  const uint32_t o = ordered_bits(kth);
-  if (o > published) {
-    atomicMax(p, o);
-    published = o;
-  }
-}
-
-// Bit j set when score j exceeds thr and is not below the shared bound (only
-// the first nvalid scores count). Four independent OR chains.
-__device__ __forceinline__ uint32_t above_mask(const uint32_t (&r)[32], float thr, float bound,
-                                               int nvalid) {
-  uint32_t m[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const float s = __uint_as_float(r[j]);
-    m[j & 3] |= ((s > thr) && (s >= bound) ? 1u : 0u) << j;
-  }
-  const uint32_t all = (m[0] | m[1]) | (m[2] | m[3]);
-  return nvalid >= 32 ? all : (all & ((1u << nvalid) - 1u));
-}
-
-// r[j] for a run-time j without indexing the register array (which would move
-// it to local memory): a 5-level select tree on the bits of j.
-__device__ __forceinline__ float pick(const uint32_t (&r)[32], int j) {
-  uint32_t l[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) l[i] = (j & 1) ? r[2 * i + 1] : r[2 * i];
-#pragma unroll
-  for (int w = 8, bit = 2; w >= 1; w >>= 1, bit <<= 1)
-#pragma unroll
-    for (int i = 0; i < w; ++i) l[i] = (j & bit) ? l[2 * i + 1] : l[2 * i];
-  return __uint_as_float(l[0]);
-}
-
-// Sorted (score desc, row asc) list of KP slots in registers holding the best
-// k <= KP candidates in its LAST k slots; the first KP-k slots are parked at
-// +inf so no finite score displaces them. The k-th best is then always the
-// last slot (a run-time slot index would push the list to local memory).
-template <int KP>
-struct EpiTopkReg {
-  // Four column stripes per quadrant for short lists (16 epilogue warps, 576
-  // threads); two for 32-slot lists, whose registers would not fit four.
-  static constexpr int kSubs = 2;
-  float tv[KP];
-  uint32_t ti[KP];
-  float thr;         // this list's k-th best (its last slot)
-  float bound;       // shared lower bound of the query (refreshed per tile)
-  uint32_t published;
-  int k;
-
-  __device__ __forceinline__ void init(const TcArgs& a) {
-    k = a.k;
-    bound = -INFINITY;
-    published = 0;
-#pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      tv[j] = (j < KP - k) ? INFINITY : -INFINITY;
-      ti[j] = 0xFFFFFFFFu;
-    }
-    thr = -INFINITY;
-  }
-
-  // The list is sorted, so "candidate ranks before slot j" is false for the
-  // leading slots and true from the insertion point on. All KP tests are
-  // independent and the shift is one select per slot: no serial chain.
-  __device__ __forceinline__ void insert(float s, uint32_t row) {
-    bool gt[KP];
-#pragma unroll
-    for (int j = 0; j < KP; ++j) gt[j] = (s > tv[j]) || (s == tv[j] && row < ti[j]);
-#pragma unroll
-    for (int j = KP - 1; j > 0; --j) {
-      tv[j] = gt[j] ? (gt[j - 1] ? tv[j - 1] : s) : tv[j];
-      ti[j] = gt[j] ? (gt[j - 1] ? ti[j - 1] : row) : ti[j];
-    }
-    tv[0] = gt[0] ? s : tv[0];
-    ti[0] = gt[0] ? row : ti[0];
-    thr = tv[KP - 1];
-  }
-
-  __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
-                                          bool qvalid, const Shared&, int) {
-    if (!qvalid) return;
-    const float mx = max32(r);
-    if (!(mx > thr && mx >= bound)) return;
-    uint32_t m = above_mask(r, thr, bound, nvalid);
-    while (m) {
-      const int j = __ffs(m) - 1;
-      m &= m - 1;
-      const float s = pick(r, j);
-      if (s > thr) insert(s, static_cast<uint32_t>(row0 + j));
-    }
-  }
-
-  __device__ __forceinline__ void finish(const TcArgs& a, int q, int list, bool qvalid, const Shared&, int) {
-    if (!qvalid) return;
-    uint64_t* out = a.part + (static_cast<size_t>(q) * a.segs * kSubs + list) * a.cap;
-#pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      if (j >= KP - k) out[j - (KP - k)] = (tv[j] == -INFINITY) ? 0ull : make_key(tv[j], ti[j]);
-    }
-  }
-};
-
-// Per-query candidate buffer of `cap` keys in global memory (L2 resident).
-// A key is appended when its score beats the current k-th best; when a list
-// could overflow on the next chunk, the warp cooperatively keeps its top k.
-struct EpiTopkBuf {
-  static constexpr int kSubs = 1;
-  uint64_t* list;
-  int cnt;
-  float thr;        // k-th best at the last compaction
-  float bound;      // shared lower bound of the query (refreshed per tile)
-  uint32_t published;
-
-  __device__ __forceinline__ void init(const TcArgs&) {
-    list = nullptr;
-    cnt = 0;
-    thr = -INFINITY;
-    bound = -INFINITY;
-    published = 0;
-  }
-
-  __device__ __forceinline__ void compact_lanes(unsigned need, const TcArgs& a, const Shared& sh,
-                                                int ew, int lane) {
-    while (need) {
-      const int src = __ffs(need) - 1;
-      need &= need - 1;
-      uint64_t* L = reinterpret_cast<uint64_t*>(shfl_u64(reinterpret_cast<uint64_t>(list), src));
-      const int m = __shfl_sync(kFullMask, cnt, src);
-      const uint64_t kth = warp_kth_key(ContigKeys{L}, m, a.k, sh.hist(ew), lane);
-      warp_compact_ge(L, m, kth, lane);
-      if (lane == src) {
-        cnt = a.k;
-        thr = key_score(kth);
-      }
-      (void)sh;
-    }
-  }
-
-  __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
-                                          bool qvalid, const Shared& sh, int ew) {
-    // `list` is set lazily so the pointer math stays out of the hot loop.
-    const float mx = max32(r);
-    if (qvalid && mx > thr && mx >= bound) {
-      uint32_t m = above_mask(r, thr, bound, nvalid);
-      while (m) {
-        const int j = __ffs(m) - 1;
-        m &= m - 1;
-        list[cnt++] = make_key(pick(r, j), static_cast<uint32_t>(row0 + j));
-      }
-    }
-    (void)sh;
-    (void)ew;
-  }
-
-  __device__ __forceinline__ void finish(const TcArgs& a, int, int, bool qvalid, const Shared& sh, int ew) {
-    const int lane = threadIdx.x & 31;
-    compact_lanes(__ballot_sync(kFullMask, qvalid && cnt > a.k), a, sh, ew, lane);
-    if (qvalid) {
-      for (int j = cnt; j < a.k; ++j) list[j] = 0ull;
-    }
-  }
-};
-
-// Writes the score tile to [b][n] (fp32 or fp16).
-template <bool F32>
-struct EpiStore {
-  static constexpr int kSubs = 2;
-  __device__ __forceinline__ void init(const TcArgs&) {}
-  __device__ __forceinline__ void consume_store(const uint32_t (&r)[32], int row0, int nvalid,
-                                                bool qvalid, const TcArgs& a, int q) {
-    if (!qvalid) return;
-    const size_t o = static_cast<size_t>(q) * a.n + row0;
-    if (F32) {
-      float* dst = reinterpret_cast<float*>(a.scores_out) + o;
-      if (nvalid == 32 && (o & 3) == 0) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j < nvalid) dst[j] = __uint_as_float(r[j]);
-      }
-    } else {
-      __half* dst = reinterpret_cast<__half*>(a.scores_out) + o;
-      if (nvalid == 32 && (o & 7) == 0) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint32_t w[4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const __half2 h = __floats2half2_rn(__uint_as_float(r[j + 2 * t]),
-                                                __uint_as_float(r[j + 2 * t + 1]));
-            w[t] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          *reinterpret_cast<uint4*>(dst + j) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j < nvalid) dst[j] = __float2half_rn(__uint_as_float(r[j]));
-      }
-    }
-  }
-};
-
-template <class E>
-struct is_store : std::false_type {};
-template <bool F>
-struct is_store<EpiStore<F>> : std::true_type {};
 
 // ---------------------------------------------------------------------------
 // The kernel
@@ -514,9 +255,9 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         if constexpr (is_store<Epi>::value) {
           epi.consume_store(r, row0 + c * 32, nv, qvalid, a, q);
         } else {
-          epi.consume(r, row0 + c * 32, nv, qvalid, sh, ew);
+          epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
           if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
-            epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a, sh, ew,
+            epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a, sh.hist(ew),
                               lane);
           }
         }
@@ -527,9 +268,29 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
       if constexpr (!is_store<Epi>::value) {
         if (qvalid) publish_bound(a.gthr + q, epi.thr, epi.published);
       }
+      if constexpr (Epi::kTops) {
+        const int lists = a.segs * Epi::kSubs;
+        const int list = seg * Epi::kSubs + sub;
+        if (qvalid) epi.publish_top(a, q, list, lists);
+        if (tops_round(t) && lists <= 32 * kTopsPerLane) {
+          // This round's refresher of each query raises the query's shared bound
+          // to the k-th largest published maximum; the whole warp serves each.
+          unsigned need = __ballot_sync(kFullMask, qvalid && tops_refresher(q, t, list, lists));
+          while (need) {
+            const int src = __ffs(need) - 1;
+            need &= need - 1;
+            const int qs = __shfl_sync(kFullMask, q, src);
+            const uint32_t kth = warp_kth_top(a.tops + static_cast<size_t>(qs) * lists, lists, a.k, lane);
+            if (lane == src && kth != 0) {
+              atomicMax(a.gthr + qs, kth);
+              epi.bound = fmaxf(epi.bound, score_of_bits(kth));
+            }
+          }
+        }
+      }
     }
     if constexpr (!is_store<Epi>::value) {
-      if (ok) epi.finish(a, q, seg * Epi::kSubs + sub, qvalid, sh, ew);
+      if (ok) epi.finish(a, q, seg * Epi::kSubs + sub, qvalid, sh.hist(ew));
     }
   }
 

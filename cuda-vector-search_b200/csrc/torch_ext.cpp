@@ -65,8 +65,8 @@ std::vector<torch::Tensor> fused_topk(torch::Tensor q, torch::Tensor x, int64_t 
   const c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(k >= 1 && k <= CVS_MAX_FUSED_K, "fused_topk supports 1 <= k <= ", CVS_MAX_FUSED_K);
   TORCH_CHECK(k <= x.size(0), "k must not exceed the corpus size");
-  TORCH_CHECK(bq == 0 || bq == 16 || bq == 32 || bq == 64 || bq == 128,
-              "bq must be 0 (auto), 16, 32, 64 or 128");
+  TORCH_CHECK(bq == 0 || bq == 16 || bq == 32 || bq == 64 || bq == 128 || bq == 256,
+              "bq must be 0 (auto), 16, 32, 64, 128 or 256");
   TORCH_CHECK(chunks >= 0 && chunks <= INT32_MAX, "chunks must be >= 0");
   const int64_t b = q.size(0), n = x.size(0);
   const int d_pad = static_cast<int>(x.size(1));
