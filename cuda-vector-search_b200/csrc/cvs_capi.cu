@@ -343,6 +343,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   m.per_list = k;
   m.k = k;
   m.id_offset = id_offset;
+  m.bounds = p.gemv ? nullptr : bounds;
   m.out_v = out_scores;
   m.out_i = reinterpret_cast<long long*>(out_ids);
   m.err = dev.err;

@@ -10,7 +10,8 @@
 //
 // One warp per row; each lane keeps its slice of the row in registers between
 // the norm and the write, so the kernel may run in place (src == dst, fp16,
-// d == d_pad, src_stride == d_pad).
+// d == d_pad, src_stride == d_pad). Rows whose width is a multiple of 8 with
+// 16-byte aligned source rows take a vectorised path (16-byte loads/stores).
 #include <cuda_bf16.h>
 
 #include "cvs_device.cuh"
@@ -70,6 +71,101 @@ __global__ void __launch_bounds__(kIngestThreads) ingest_kernel(const void* src,
   }
 }
 
+// Vectorised variant for d % 8 == 0 with 16-byte aligned source rows: lane l
+// handles 8-element chunks l, l+32, ... (CPL of them), read with 16/32/64-byte
+// loads and written as one 16-byte store each.
+template <int T>
+struct Chunk8 {
+  static __device__ __forceinline__ void load(const void* src, size_t e, __half (&h)[8]) {
+    if constexpr (T == kSrcF16 || T == kSrcBF16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(src) + e);
+      const uint16_t* w = reinterpret_cast<const uint16_t*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if constexpr (T == kSrcF16) h[j] = __ushort_as_half(w[j]);
+        else h[j] = __float2half_rn(__bfloat162float(__ushort_as_bfloat16(w[j])));
+      }
+    } else if constexpr (T == kSrcF32) {
+      const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(src) + e);
+      const float4 a = f[0], b = f[1];
+      h[0] = __float2half_rn(a.x); h[1] = __float2half_rn(a.y); h[2] = __float2half_rn(a.z); h[3] = __float2half_rn(a.w);
+      h[4] = __float2half_rn(b.x); h[5] = __float2half_rn(b.y); h[6] = __float2half_rn(b.z); h[7] = __float2half_rn(b.w);
+    } else {
+      const double2* f = reinterpret_cast<const double2*>(static_cast<const double*>(src) + e);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const double2 v = f[j];
+        h[2 * j] = __double2half(v.x);
+        h[2 * j + 1] = __double2half(v.y);
+      }
+    }
+  }
+};
+
+template <int T, int CPL>
+__global__ void __launch_bounds__(kIngestThreads) ingest_vec_kernel(const void* src, long long n, int d,
+                                                                    long long src_stride, int d_pad,
+                                                                    int cosine, __half* dst) {
+  const int lane = threadIdx.x & 31;
+  const int dchunks = d >> 3, pchunks = d_pad >> 3;
+  const long long warps = static_cast<long long>(gridDim.x) * (kIngestThreads / 32);
+  for (long long row = static_cast<long long>(blockIdx.x) * (kIngestThreads / 32) + (threadIdx.x >> 5);
+       row < n; row += warps) {
+    __half h[CPL][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < dchunks) {
+        Chunk8<T>::load(src, static_cast<size_t>(row) * src_stride + static_cast<size_t>(c) * 8, h[j]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) h[j][t] = __float2half_rn(0.f);
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float f = __half2float(h[j][t]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+    float den = 1.f;
+    if (cosine) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      den = fmaxf(sqrtf(ss), 1e-12f);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const int c = lane + 32 * j;
+      if (c < pchunks) {
+        uint4 o;
+        __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          oh[t] = cosine ? __float2half_rn(__fdiv_rn(__half2float(h[j][t]), den)) : h[j][t];
+        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(row) * d_pad + static_cast<size_t>(c) * 8) = o;
+      }
+    }
+  }
+}
+
+template <int T>
+cudaError_t launch_vec(const void* src, long long n, int d, long long src_stride, int d_pad, int cosine,
+                       __half* dst, unsigned grid, cudaStream_t stream) {
+  const int cpl = (d_pad / 8 + 31) / 32;
+#define CVS_INGEST_VEC(C)                                                                          \
+  if (cpl <= C) {                                                                                 \
+    ingest_vec_kernel<T, C><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); \
+    return cudaGetLastError();                                                                     \
+  }
+  CVS_INGEST_VEC(1) CVS_INGEST_VEC(2) CVS_INGEST_VEC(3) CVS_INGEST_VEC(4) CVS_INGEST_VEC(6) CVS_INGEST_VEC(8)
+#undef CVS_INGEST_VEC
+  return cudaErrorInvalidValue;
+}
+
+size_t elem_size(int t) { return t == kSrcF32 ? 4 : t == kSrcF64 ? 8 : 2; }
+
 }  // namespace
 
 cudaError_t ingest_launch(const void* src, int src_dtype, long long n, int d, long long src_stride,
@@ -78,6 +174,18 @@ cudaError_t ingest_launch(const void* src, int src_dtype, long long n, int d, lo
   if (n == 0) return cudaSuccess;
   const long long want = (n + (kIngestThreads / 32) - 1) / (kIngestThreads / 32);
   const unsigned grid = static_cast<unsigned>(std::min<long long>(want, static_cast<long long>(num_sms) * 8));
+  const size_t es = elem_size(src_dtype);
+  const bool vec = d % 8 == 0 && d_pad <= 2048 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+                   (static_cast<size_t>(src_stride) * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+  if (vec) {
+    switch (src_dtype) {
+      case kSrcF32: return launch_vec<kSrcF32>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
+      case kSrcF16: return launch_vec<kSrcF16>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
+      case kSrcBF16: return launch_vec<kSrcBF16>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
+      case kSrcF64: return launch_vec<kSrcF64>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (src_dtype) {
     case kSrcF32: ingest_kernel<kSrcF32><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); break;
     case kSrcF16: ingest_kernel<kSrcF16><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); break;

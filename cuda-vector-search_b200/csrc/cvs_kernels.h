@@ -87,6 +87,7 @@ struct MergeKeysArgs {
   int per_list;
   int k;
   long long id_offset;   // added to every returned row id
+  const uint32_t* bounds;  // [b] lower bounds on each query's k-th best (ordered bits) or null
   float* out_v;          // [b][k]
   long long* out_i;      // [b][k]
   int* err;

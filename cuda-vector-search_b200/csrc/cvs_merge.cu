@@ -19,14 +19,21 @@ namespace cvs {
 
 namespace {
 
-constexpr int kMergeWarps = 4;
+constexpr int kMergeWarps = 2;
 constexpr int kMergeMaxK = 1024;
+constexpr int kSurvivorCap = 512;
+
+// Shared memory per warp: radix histogram, k selected keys, survivor buffer.
+__host__ __device__ constexpr size_t merge_warp_bytes(int k) {
+  return 256 * 4 + static_cast<size_t>(k) * 8 + static_cast<size_t>(kSurvivorCap) * 8;
+}
 
 struct PartKeys {
   const uint64_t* p;  // this query's [lists][stride] block
   int stride;
   int per_list;
   __device__ __forceinline__ uint64_t operator()(int i) const {
+    if (stride == per_list) return p[i];
     return p[static_cast<size_t>(i / per_list) * stride + (i % per_list)];
   }
 };
@@ -84,19 +91,47 @@ __device__ void select_and_emit(const Acc& acc, int m, int k, long long id_offse
   __syncwarp();
 }
 
+// Per query: when the search kernel left a lower bound on the query's k-th best
+// score (a.bounds), one coalesced pass keeps only the keys at or above it --
+// typically a few times k of the lists*k keys -- in shared memory, and the
+// selection runs there. Without a bound, or if more than kSurvivorCap keys
+// survive, the selection runs over all keys.
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_keys_kernel(const MergeKeysArgs a) {
   extern __shared__ uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int q = blockIdx.x * kMergeWarps + warp;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + 256 * warp;
-  uint64_t* sel = reinterpret_cast<uint64_t*>(smem + kMergeWarps * 256 * 4) +
-                  static_cast<size_t>(warp) * a.k;
+  uint8_t* mine = smem + static_cast<size_t>(warp) * merge_warp_bytes(a.k);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(mine);
+  uint64_t* sel = reinterpret_cast<uint64_t*>(mine + 256 * 4);
+  uint64_t* surv = sel + a.k;
   if (q >= a.b) return;  // whole warp
   const PartKeys acc{a.part + static_cast<size_t>(q) * a.lists * a.stride, a.stride, a.per_list};
-  select_and_emit(acc, a.lists * a.per_list, a.k, a.id_offset, hist, sel,
-                  a.out_v + static_cast<size_t>(q) * a.k, a.out_i + static_cast<size_t>(q) * a.k,
-                  lane);
+  const int m = a.lists * a.per_list;
+  float* out_v = a.out_v + static_cast<size_t>(q) * a.k;
+  long long* out_i = a.out_i + static_cast<size_t>(q) * a.k;
+  if (a.bounds != nullptr) {
+    uint32_t bound;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(bound) : "l"(a.bounds + q));
+    int cnt = 0;
+    for (int i0 = 0; i0 < m; i0 += 32) {
+      const int i = i0 + lane;
+      const uint64_t key = i < m ? acc(i) : 0ull;
+      const bool keep = key != 0ull && static_cast<uint32_t>(key >> 32) >= bound;
+      const unsigned bal = __ballot_sync(kFullMask, keep);
+      if (keep) {
+        const int pos = cnt + __popc(bal & ((1u << lane) - 1u));
+        if (pos < kSurvivorCap) surv[pos] = key;
+      }
+      cnt += __popc(bal);
+    }
+    __syncwarp();
+    if (cnt <= kSurvivorCap) {
+      select_and_emit(ContigKeys{surv}, cnt, a.k, a.id_offset, hist, sel, out_v, out_i, lane);
+      return;
+    }
+  }
+  select_and_emit(acc, m, a.k, a.id_offset, hist, sel, out_v, out_i, lane);
 }
 
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const MergeListsArgs a) {
@@ -104,16 +139,16 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const Mer
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int q = blockIdx.x * kMergeWarps + warp;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + 256 * warp;
-  uint64_t* sel = reinterpret_cast<uint64_t*>(smem + kMergeWarps * 256 * 4) +
-                  static_cast<size_t>(warp) * a.k;
+  uint8_t* mine = smem + static_cast<size_t>(warp) * merge_warp_bytes(a.k);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(mine);
+  uint64_t* sel = reinterpret_cast<uint64_t*>(mine + 256 * 4);
   if (q >= a.b) return;
   const ListKeys acc{a.v, a.ids, a.b, a.len, q};
   select_and_emit(acc, a.lists * a.len, a.k, 0, hist, sel, a.out_v + static_cast<size_t>(q) * a.k,
                   a.out_i + static_cast<size_t>(q) * a.k, lane);
 }
 
-size_t merge_smem(int k) { return kMergeWarps * (256 * 4 + static_cast<size_t>(k) * 8); }
+size_t merge_smem(int k) { return kMergeWarps * merge_warp_bytes(k); }
 
 }  // namespace
 
