@@ -195,8 +195,8 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->segs = static_cast<int>((n + p->rows_per_seg - 1) / p->rows_per_seg);
     p->cap = k;
     p->lists = p->segs;
-    p->bound_bytes = 0;
-    p->ws_bytes = round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
+    p->bound_bytes = round_up(static_cast<size_t>(b) * 4 * (1 + p->lists), kWsAlign);
+    p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
     return CVS_OK;
   }
   p->gemv = false;
@@ -296,7 +296,8 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   const bool prof = g_prof_start && g_prof_stop;
   cudaError_t e;
   // The shared per-query bounds must start at "none" (0) on every call.
-  if (p.bound_bytes && (e = cudaMemsetAsync(bounds, 0, static_cast<size_t>(b) * 4 * (1 + p.lists), s)) != cudaSuccess)
+  const size_t clear_bytes = static_cast<size_t>(b) * 4 * (1 + p.lists);
+  if (p.bound_bytes && (e = cudaMemsetAsync(bounds, 0, clear_bytes, s)) != cudaSuccess)
     return cuda_fail(e, "clearing the per-query bounds");
   if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   if (p.gemv) {
@@ -310,6 +311,8 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     a.segs = p.segs;
     a.rows_per_seg = p.rows_per_seg;
     a.part = part;
+    a.bounds = bounds;
+    a.tops = bounds + b;
     a.err = dev.err;
     if ((e = gemv_launch(a, s)) != cudaSuccess) return cuda_fail(e, "gemv top-k launch");
   } else {
@@ -343,7 +346,11 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   m.per_list = k;
   m.k = k;
   m.id_offset = id_offset;
-  m.bounds = p.gemv ? nullptr : bounds;
+  m.bounds = bounds;
+  // Register top-k lists and GEMV CTAs publish their best scores; the buffer
+  // epilogue does not.
+  m.tops = (p.gemv || p.epi != kEpiTopkBuf) ? bounds + b : nullptr;
+  m.tops_n = p.lists;
   m.out_v = out_scores;
   m.out_i = reinterpret_cast<long long*>(out_ids);
   m.err = dev.err;

@@ -93,32 +93,7 @@ __device__ __forceinline__ float pick(const uint32_t (&r)[32], int j) {
   return __uint_as_float(l[0]);
 }
 
-// k-th largest of the published maxima a.tops[q][0..lists) (ordered bits, 0 =
-// none), computed by the whole warp: each lane loads up to kTopsPerLane of them
-// (one round trip), then a 32-step bisection on the value bits with warp-wide
-// counts finds the largest v such that at least k maxima are >= v. Returns 0
-// when fewer than k lists have published.
-constexpr int kTopsPerLane = 10;  // lists per query <= 320
-
-__device__ __forceinline__ uint32_t warp_kth_top(const uint32_t* row, int lists, int k, int lane) {
-  uint32_t v[kTopsPerLane];
-#pragma unroll
-  for (int j = 0; j < kTopsPerLane; ++j) {
-    const int i = lane + 32 * j;
-    v[j] = 0;
-    if (i < lists) asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v[j]) : "l"(row + i));
-  }
-  uint32_t prefix = 0;
-#pragma unroll 1
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t cand = prefix | (1u << bit);
-    uint32_t c = 0;
-#pragma unroll
-    for (int j = 0; j < kTopsPerLane; ++j) c += v[j] >= cand ? 1u : 0u;
-    if (__reduce_add_sync(kFullMask, c) >= static_cast<uint32_t>(k)) prefix = cand;
-  }
-  return prefix;
-}
+constexpr int kTopsPerLane = 10;  // lists per query <= 320 for the in-kernel refresh
 
 // Sorted (score desc, row asc) list of KP slots in registers holding the best
 // k <= KP candidates in its LAST k slots; the first KP-k slots are parked at

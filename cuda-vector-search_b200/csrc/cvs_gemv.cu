@@ -14,6 +14,10 @@
 // the j-th best). A new candidate finds its slot with one ballot and the lanes
 // below it shift down by one with one shuffle. At the end the CTA merges its
 // warps' lists with the warp radix select and writes k keys per query.
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "cvs_device.cuh"
 #include "cvs_kernels.h"
 #include "cvs_select.cuh"
@@ -151,6 +155,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_topk_kernel(const GemvArgs 
       __device__ uint64_t operator()(int i) const { return p[(i / k) * kGemvMaxK + (i % k)]; }
     } acc{base, kk};
     const uint64_t kth = warp_kth_key(acc, m, kk, hist[warp], lane);
+    // This CTA's k-th best bounds the query's k-th best from below; the merge
+    // uses the largest such bound to skip most candidates.
+    if (lane == 0 && kth != 0ull) atomicMax(a.bounds + qi, static_cast<uint32_t>(kth >> 32));
+    // ... and its best score is published for the merge's k-th-largest-maximum bound.
+    uint64_t best = 0ull;
+    for (int i = lane; i < m; i += 32) best = max(best, acc(i));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) best = max(best, shfl_u64(best, lane ^ off));
+    if (lane == 0) a.tops[static_cast<size_t>(qi) * a.segs + blockIdx.x] = static_cast<uint32_t>(best >> 32);
     uint64_t* out = a.part + (static_cast<size_t>(qi) * a.segs + blockIdx.x) * kk;
     // Emit keys >= kth (exactly k when kth != 0); pad with empty keys otherwise.
     int pos = 0;
@@ -204,10 +217,20 @@ bool gemv_supported(int b, int k, int d_pad) {
 // grid is exactly one full wave.
 int gemv_blocks_per_sm(int b, int d_pad) {
   GemvKernel k = select_kernel(b, d_pad);
+  if (!k) return 1;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> cache;  // (device, kernel) -> blocks
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(k));
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
   int blocks = 0;
-  if (!k || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, kGemvThreads, 0) != cudaSuccess)
-    return 1;
-  return blocks > 0 ? blocks : 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, kGemvThreads, 0) != cudaSuccess) blocks = 1;
+  blocks = blocks > 0 ? blocks : 1;
+  cache.emplace(key, blocks);
+  return blocks;
 }
 
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t stream) {

@@ -71,6 +71,8 @@ struct GemvArgs {
   int segs;           // grid size; segment s covers rows [s*rows_per_seg, ...)
   int rows_per_seg;
   uint64_t* part;     // [b][segs][k]
+  uint32_t* bounds;   // [b] per-query lower bounds on the k-th best (ordered bits), zeroed per call
+  uint32_t* tops;     // [b][segs] each CTA's best score (ordered bits)
   int* err;
 };
 
@@ -88,6 +90,8 @@ struct MergeKeysArgs {
   int k;
   long long id_offset;   // added to every returned row id
   const uint32_t* bounds;  // [b] lower bounds on each query's k-th best (ordered bits) or null
+  const uint32_t* tops;    // [b][tops_n] per-list best scores (ordered bits, 0 = none) or null
+  int tops_n;
   float* out_v;          // [b][k]
   long long* out_i;      // [b][k]
   int* err;

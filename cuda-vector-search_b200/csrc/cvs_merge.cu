@@ -22,6 +22,7 @@ namespace {
 constexpr int kMergeWarps = 2;
 constexpr int kMergeMaxK = 1024;
 constexpr int kSurvivorCap = 512;
+constexpr int kMergeTopsPerLane = 16;  // up to 512 lists per query
 
 // Shared memory per warp: radix histogram, k selected keys, survivor buffer.
 __host__ __device__ constexpr size_t merge_warp_bytes(int k) {
@@ -113,17 +114,30 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_keys_kernel(const Merg
   if (a.bounds != nullptr) {
     uint32_t bound;
     asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(bound) : "l"(a.bounds + q));
+    // The k-th largest of the lists' final best scores is usually a much
+    // tighter bound than the kernel's running one.
+    if (a.tops != nullptr && a.tops_n <= 32 * kMergeTopsPerLane)
+      bound = max(bound, warp_kth_top<kMergeTopsPerLane>(a.tops + static_cast<size_t>(q) * a.tops_n,
+                                                         a.tops_n, a.k, lane));
     int cnt = 0;
-    for (int i0 = 0; i0 < m; i0 += 32) {
-      const int i = i0 + lane;
-      const uint64_t key = i < m ? acc(i) : 0ull;
-      const bool keep = key != 0ull && static_cast<uint32_t>(key >> 32) >= bound;
-      const unsigned bal = __ballot_sync(kFullMask, keep);
-      if (keep) {
-        const int pos = cnt + __popc(bal & ((1u << lane) - 1u));
-        if (pos < kSurvivorCap) surv[pos] = key;
+    constexpr int kBatch = 8;  // loads in flight per lane before any is used
+    for (int i0 = 0; i0 < m; i0 += 32 * kBatch) {
+      uint64_t keys[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + 32 * u + lane;
+        keys[u] = i < m ? acc(i) : 0ull;
       }
-      cnt += __popc(bal);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const bool keep = keys[u] != 0ull && static_cast<uint32_t>(keys[u] >> 32) >= bound;
+        const unsigned bal = __ballot_sync(kFullMask, keep);
+        if (keep) {
+          const int pos = cnt + __popc(bal & ((1u << lane) - 1u));
+          if (pos < kSurvivorCap) surv[pos] = keys[u];
+        }
+        cnt += __popc(bal);
+      }
     }
     __syncwarp();
     if (cnt <= kSurvivorCap) {

@@ -51,9 +51,18 @@ __device__ uint64_t warp_kth_key(const Acc& acc, int m, int k, uint32_t* hist, i
   for (int shift = 56; shift >= 0; shift -= 8) {
     for (int i = lane; i < 256; i += 32) hist[i] = 0u;
     __syncwarp();
-    for (int i = lane; i < m; i += 32) {
-      const uint64_t key = acc(i);
-      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    for (int i0 = 0; i0 < m; i0 += 128) {  // four loads in flight per lane
+      uint64_t key[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + 32 * u + lane;
+        key[u] = i < m ? acc(i) : 0ull;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (i0 + 32 * u + lane < m && (key[u] & pmask) == prefix)
+          atomicAdd(&hist[(key[u] >> shift) & 255u], 1u);
+      }
     }
     __syncwarp();
     // Lane l owns bins 255-8l .. 248-8l, visited from the highest digit down.
@@ -123,6 +132,34 @@ __device__ __forceinline__ int warp_compact_ge(uint64_t* list, int m, uint64_t k
   }
   __syncwarp();
   return base;
+}
+
+// k-th largest of n published per-list maxima row[0..n) (ordered score bits,
+// 0 = none), computed by the whole warp: each lane loads up to PER_LANE of them
+// in one round trip, then a 32-step bisection on the value bits with warp-wide
+// counts finds the largest v such that at least k maxima are >= v. If k lists
+// hold a score >= v, at least k rows score >= v, so v bounds the query's k-th
+// best from below. Returns 0 when fewer than k lists have published.
+// Requires n <= 32 * PER_LANE.
+template <int PER_LANE>
+__device__ __forceinline__ uint32_t warp_kth_top(const uint32_t* row, int n, int k, int lane) {
+  uint32_t v[PER_LANE];
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int i = lane + 32 * j;
+    v[j] = 0;
+    if (i < n) asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v[j]) : "l"(row + i));
+  }
+  uint32_t prefix = 0;
+#pragma unroll 1
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = prefix | (1u << bit);
+    uint32_t c = 0;
+#pragma unroll
+    for (int j = 0; j < PER_LANE; ++j) c += v[j] >= cand ? 1u : 0u;
+    if (__reduce_add_sync(kFullMask, c) >= static_cast<uint32_t>(k)) prefix = cand;
+  }
+  return prefix;
 }
 
 }  // namespace cvs

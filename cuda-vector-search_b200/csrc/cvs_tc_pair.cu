@@ -291,7 +291,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
             const int src = __ffs(need) - 1;
             need &= need - 1;
             const int qs = __shfl_sync(kFullMask, q, src);
-            const uint32_t kth = warp_kth_top(a.tops + static_cast<size_t>(qs) * lists, lists, a.k, lane);
+            const uint32_t kth = warp_kth_top<kTopsPerLane>(a.tops + static_cast<size_t>(qs) * lists, lists, a.k, lane);
             if (lane == src && kth != 0) {
               atomicMax(a.gthr + qs, kth);
               epi.bound = fmaxf(epi.bound, score_of_bits(kth));

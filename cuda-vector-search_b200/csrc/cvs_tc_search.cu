@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
             const int src = __ffs(need) - 1;
             need &= need - 1;
             const int qs = __shfl_sync(kFullMask, q, src);
-            const uint32_t kth = warp_kth_top(a.tops + static_cast<size_t>(qs) * lists, lists, a.k, lane);
+            const uint32_t kth = warp_kth_top<kTopsPerLane>(a.tops + static_cast<size_t>(qs) * lists, lists, a.k, lane);
             if (lane == src && kth != 0) {
               atomicMax(a.gthr + qs, kth);
               epi.bound = fmaxf(epi.bound, score_of_bits(kth));
