@@ -23,7 +23,7 @@ import torch
 import torch.distributed as dist
 
 from . import _ext
-from .index import Index
+from .index import MAX_FUSED_K, Index
 
 
 def all_gather_stacked(t: torch.Tensor, group=None) -> torch.Tensor:
@@ -117,6 +117,8 @@ class ShardedIndex:
         if k < 1:
             raise ValueError("k must be >= 1")
         k = min(k, self.n_total)
+        if k > MAX_FUSED_K:
+            raise ValueError(f"sharded search supports k <= {MAX_FUSED_K}")
         v, i = self.ops.local_topk(queries, k, self.row_offset)
         v_all = all_gather_stacked(v, self.group)
         i_all = all_gather_stacked(i, self.group)

@@ -1,0 +1,72 @@
+"""Sharded search on the GPU.
+
+* Simulated on one GPU: the corpus is split into S pseudo-shards, each searched
+  with its global row offset (fused_topk_into), the [S, b, k] lists merged with
+  merge_lists; the result must equal the unsharded search exactly.
+* Real ranks: when at least two GPUs are visible, tests/mp_sharded_check.py runs
+  under torchrun with NCCL and compares ShardedIndex with a single-GPU Index.
+"""
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def mod():
+    from cuda_vector_search import _ext
+
+    assert _ext.available()
+    return _ext.load()
+
+
+@pytest.mark.parametrize("n,d,b,k,shards", [(20000, 384, 64, 10, 4), (20000, 768, 300, 32, 3),
+                                            (9000, 128, 5, 100, 7), (5000, 256, 1, 10, 2)])
+def test_simulated_sharding_equals_unsharded(mod, n, d, b, k, shards):
+    import cuda_vector_search as cvs
+
+    g = torch.Generator().manual_seed(n + b)
+    x = torch.randn(n, d, generator=g).half().cuda()
+    q = torch.randn(b, d, generator=g).half().cuda()
+    full = cvs.Index(x, metric="cosine")
+    ref_v, ref_i = full.search(q, k)
+    bounds = [round(s * n / shards) for s in range(shards + 1)]
+    vs, ids = [], []
+    for s in range(shards):
+        part = cvs.Index(x[bounds[s]:bounds[s + 1]], metric="cosine")
+        qq = part._prep_queries(q)
+        kk = min(k, len(part))
+        v = torch.empty(b, kk, device="cuda")
+        i = torch.empty(b, kk, dtype=torch.int64, device="cuda")
+        ws = torch.empty(max(256, mod.workspace_size(b, len(part), part._x.shape[1], kk)), dtype=torch.uint8,
+                         device="cuda")
+        mod.fused_topk_into(qq, part._x, kk, bounds[s], v, i, ws)
+        if kk < k:
+            v = torch.cat([v, v.new_full((b, k - kk), float("-inf"))], 1)
+            i = torch.cat([i, i.new_full((b, k - kk), -1)], 1)
+        vs.append(v)
+        ids.append(i)
+    mv, mi = mod.merge_lists(torch.stack(vs).contiguous(), torch.stack(ids).contiguous(), k)
+    assert torch.equal(mi, ref_i)
+    assert torch.allclose(mv, ref_v, atol=1e-6, rtol=0)
+
+
+def test_nccl_ranks_match_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(ROOT), str(ROOT / "cuda-vector-search_b200"),
+                                                        os.environ.get("PYTHONPATH", "")]))
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533",
+           str(ROOT / "tests" / "mp_sharded_check.py")]
+    res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=360)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert "SHARDED OK" in res.stdout
