@@ -168,11 +168,11 @@ void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks, int epi, i
   int slots;
   if (p->pair) {
     p->qtiles = static_cast<int>((b + 2 * kTcM - 1) / (2 * kTcM));
-    p->qres = tc_pair_resident_queries(ksl);
+    p->qres = tc_pair_resident_queries(epi, ksl);
     slots = pair_clusters(epi, p->qres, ksl, sms);
   } else {
     p->qtiles = static_cast<int>((b + kTcM - 1) / kTcM);
-    p->qres = ksl <= kTcMaxResidentSlices;
+    p->qres = tc_resident_queries(epi, ksl);
     slots = sms;
   }
   int segs = chunks > 0 ? chunks : std::max(1, slots / std::max(1, p->qtiles));
@@ -349,8 +349,16 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   m.bounds = bounds;
   // Register top-k lists and GEMV CTAs publish their best scores; the buffer
   // epilogue does not.
-  m.tops = (p.gemv || p.epi != kEpiTopkBuf) ? bounds + b : nullptr;
+  m.tops = bounds + b;
   m.tops_n = p.lists;
+  // Register lists and GEMV CTAs publish their best score (m = k lists needed);
+  // buffer lists publish their J-th best with J = ceil(2k / lists) (m = ceil(k / J)).
+  if (!p.gemv && p.epi == kEpiTopkBuf) {
+    const int j = std::min(k, std::max(1, (2 * k + p.lists - 1) / p.lists));
+    m.tops_m = (k + j - 1) / j;
+  } else {
+    m.tops_m = k;
+  }
   m.out_v = out_scores;
   m.out_i = reinterpret_cast<long long*>(out_ids);
   m.err = dev.err;

@@ -104,6 +104,7 @@ struct EpiTopkReg {
   // Two column stripes per TMEM quadrant (8 epilogue warps, 320 threads).
   static constexpr int kSubs = 2;
   static constexpr bool kTops = true;
+  static constexpr int kScratchKeys = 0;
   float tv[KP];
   uint32_t ti[KP];
   float thr;         // this list's k-th best (its last slot)
@@ -175,7 +176,10 @@ struct EpiTopkReg {
     }
   }
 
-  __device__ __forceinline__ void finish(const TcArgs& a, int q, int list, bool qvalid, uint32_t*) {
+  static __device__ __forceinline__ int jrank(int, int) { return 1; }  // publishes its best
+
+  __device__ __forceinline__ void finish(const TcArgs& a, int q, int list, bool qvalid, uint32_t*, uint64_t*,
+                                         int) {
     if (!qvalid) return;
     uint64_t* out = a.part + (static_cast<size_t>(q) * a.segs * kSubs + list) * a.cap;
 #pragma unroll
@@ -188,41 +192,105 @@ struct EpiTopkReg {
 // Per-query candidate buffer of `cap` keys in global memory (L2 resident).
 // A key is appended when its score beats the current k-th best; when a list
 // could overflow on the next chunk, the warp cooperatively keeps its top k.
+// Rank of the per-list value a list publishes (its J-th best) and how many lists
+// must reach a value for it to bound the query's k-th best (m lists x J rows
+// >= k rows). With at least 2k lists this is (1, k): every list publishes its
+// best. The merge uses the same pair.
+__host__ __device__ __forceinline__ int tops_j(int k, int lists) {
+  const int j = (2 * k + lists - 1) / max(1, lists);
+  return j < 1 ? 1 : (j > k ? k : j);
+}
+__host__ __device__ __forceinline__ int tops_m(int k, int lists) {
+  const int j = tops_j(k, lists);
+  return (k + j - 1) / j;
+}
+
+// Per-query candidate buffer of `cap` keys in global memory (L2 resident) for
+// k > 32. A key is appended when its score beats the list's k-th best (as of
+// its last compaction) and the query's shared bound; when a list could
+// overflow on the next chunk, the warp loads it into shared memory in one round
+// trip, radix-selects its top k and J-th best there, writes the top k back and
+// publishes the J-th best for the query's bound.
 struct EpiTopkBuf {
   static constexpr int kSubs = 1;
-  static constexpr bool kTops = false;
+  static constexpr bool kTops = true;
+  static constexpr int kScratchKeys = 512;  // shared-memory compaction up to cap 512 (k <= 256)
+  static __device__ __forceinline__ int jrank(int k, int lists) { return tops_j(k, lists); }
   uint64_t* list;
   int cnt;
   float thr;        // k-th best at the last compaction
   float bound;      // shared lower bound of the query (refreshed per tile)
+  float best;       // value this list publishes: its J-th best at the last compaction
   uint32_t published;
+  uint32_t top_published;
 
   __device__ __forceinline__ void init(const TcArgs&) {
     list = nullptr;
     cnt = 0;
     thr = -INFINITY;
     bound = -INFINITY;
+    best = -INFINITY;
     published = 0;
+    top_published = 0;
   }
 
-  __device__ __forceinline__ void compact_lanes(unsigned need, const TcArgs& a, uint32_t* hist, int lane) {
-    while (need) {
-      const int src = __ffs(need) - 1;
-      need &= need - 1;
-      uint64_t* L = reinterpret_cast<uint64_t*>(shfl_u64(reinterpret_cast<uint64_t>(list), src));
-      const int m = __shfl_sync(kFullMask, cnt, src);
-      const uint64_t kth = warp_kth_key(ContigKeys{L}, m, a.k, hist, lane);
+  // Keeps the top min(k, m) keys of lane src's list and records its k-th best
+  // and J-th best; scratch = this warp's shared buffer (kScratchKeys keys).
+  __device__ __forceinline__ void compact_one(int src, const TcArgs& a, int jrank, uint32_t* hist,
+                                              uint64_t* scratch, int lane) {
+    uint64_t* L = reinterpret_cast<uint64_t*>(shfl_u64(reinterpret_cast<uint64_t>(list), src));
+    const int m = __shfl_sync(kFullMask, cnt, src);
+    uint64_t kth = 0, jth = 0;
+    if (m <= kScratchKeys) {
+      constexpr int kPerLane = kScratchKeys / 32;
+      uint64_t v[kPerLane];
+#pragma unroll
+      for (int u = 0; u < kPerLane; ++u) {
+        const int i = lane + 32 * u;
+        v[u] = i < m ? L[i] : 0ull;
+      }
+#pragma unroll
+      for (int u = 0; u < kPerLane; ++u) scratch[lane + 32 * u] = v[u];
+      __syncwarp();
+      if (m > a.k) {
+        kth = warp_kth_key(ContigKeys{scratch}, m, a.k, hist, lane);
+        int base = 0;
+        for (int i0 = 0; i0 < m; i0 += 32) {
+          const int i = i0 + lane;
+          const uint64_t key = i < m ? scratch[i] : 0ull;
+          const bool keep = i < m && key >= kth;
+          const unsigned bal = __ballot_sync(kFullMask, keep);
+          if (keep) L[base + __popc(bal & ((1u << lane) - 1u))] = key;
+          base += __popc(bal);
+        }
+      }
+      if (m >= jrank) jth = warp_kth_key(ContigKeys{scratch}, m, jrank, hist, lane);
+      __syncwarp();
+    } else {
+      kth = warp_kth_key(ContigKeys{L}, m, a.k, hist, lane);
       warp_compact_ge(L, m, kth, lane);
-      if (lane == src) {
+      jth = warp_kth_key(ContigKeys{L}, a.k, jrank, hist, lane);
+    }
+    if (lane == src) {
+      if (m > a.k) {
         cnt = a.k;
         thr = key_score(kth);
       }
+      if (jth != 0ull) best = fmaxf(best, key_score(jth));
+    }
+  }
+
+  __device__ __forceinline__ void compact_lanes(unsigned need, const TcArgs& a, int jrank, uint32_t* hist,
+                                                uint64_t* scratch, int lane) {
+    while (need) {
+      const int src = __ffs(need) - 1;
+      need &= need - 1;
+      compact_one(src, a, jrank, hist, scratch, lane);
     }
   }
 
   __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
-                                          bool qvalid, uint32_t* hist) {
-    // `list` is set lazily so the pointer math stays out of the hot loop.
+                                          bool qvalid, uint32_t*) {
     const float mx = max32(r);
     if (qvalid && mx > thr && mx >= bound) {
       uint32_t m = above_mask(r, thr, bound, nvalid);
@@ -232,14 +300,28 @@ struct EpiTopkBuf {
         list[cnt++] = make_key(pick(r, j), static_cast<uint32_t>(row0 + j));
       }
     }
-    (void)hist;
   }
 
-  __device__ __forceinline__ void finish(const TcArgs& a, int, int, bool qvalid, uint32_t* hist) {
+  __device__ __forceinline__ void publish_top(const TcArgs& a, int q, int list_idx, int lists) {
+    if (best == -INFINITY) return;
+    const uint32_t o = ordered_bits(best);
+    if (o > top_published) {
+      asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(a.tops + static_cast<size_t>(q) * lists + list_idx),
+                   "r"(o)
+                   : "memory");
+      top_published = o;
+    }
+  }
+
+  __device__ __forceinline__ void finish(const TcArgs& a, int q, int list_idx, bool qvalid, uint32_t* hist,
+                                         uint64_t* scratch, int lists) {
     const int lane = threadIdx.x & 31;
-    compact_lanes(__ballot_sync(kFullMask, qvalid && cnt > a.k), a, hist, lane);
+    const int jrank = tops_j(a.k, lists);
+    compact_lanes(__ballot_sync(kFullMask, qvalid && (cnt > a.k || cnt >= jrank)), a, jrank, hist, scratch,
+                  lane);
     if (qvalid) {
       for (int j = cnt; j < a.k; ++j) list[j] = 0ull;
+      publish_top(a, q, list_idx, lists);
     }
   }
 };
@@ -249,6 +331,7 @@ template <bool F32>
 struct EpiStore {
   static constexpr int kSubs = 2;
   static constexpr bool kTops = false;
+  static constexpr int kScratchKeys = 0;
   __device__ __forceinline__ void init(const TcArgs&) {}
   __device__ __forceinline__ void consume_store(const uint32_t (&r)[32], int row0, int nvalid,
                                                 bool qvalid, const TcArgs& a, int q) {

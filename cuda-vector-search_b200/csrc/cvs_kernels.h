@@ -47,12 +47,15 @@ struct TcArgs {
 // Candidate lists each (query, segment) produces with this epilogue (one per
 // epilogue column stripe); the workspace holds b * segs * lists * cap keys.
 int tc_lists_per_segment(int epi);
+// Whether the query tile can stay resident in shared memory next to the stage
+// ring and this epilogue's scratch (one-CTA kernel).
+bool tc_resident_queries(int epi, int ksl);
 cudaError_t tc_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                       const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
 
 // CTA-pair variant (batches > 128): a.qtiles counts 256-query pair tiles, the
 // corpus tensor map uses 128-row boxes, the grid is 2 * qtiles * segs CTAs.
-bool tc_pair_resident_queries(int ksl);
+bool tc_pair_resident_queries(int epi, int ksl);
 int tc_pair_max_clusters(int epi, bool resident_queries, int ksl);
 cudaError_t tc_pair_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                            const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
@@ -90,8 +93,9 @@ struct MergeKeysArgs {
   int k;
   long long id_offset;   // added to every returned row id
   const uint32_t* bounds;  // [b] lower bounds on each query's k-th best (ordered bits) or null
-  const uint32_t* tops;    // [b][tops_n] per-list best scores (ordered bits, 0 = none) or null
+  const uint32_t* tops;    // [b][tops_n] per-list published scores (ordered bits, 0 = none) or null
   int tops_n;
+  int tops_m;              // the tops_m-th largest published score bounds the k-th best
   float* out_v;          // [b][k]
   long long* out_i;      // [b][k]
   int* err;

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_keys_kernel(const Merg
     // tighter bound than the kernel's running one.
     if (a.tops != nullptr && a.tops_n <= 32 * kMergeTopsPerLane)
       bound = max(bound, warp_kth_top<kMergeTopsPerLane>(a.tops + static_cast<size_t>(q) * a.tops_n,
-                                                         a.tops_n, a.k, lane));
+                                                         a.tops_n, a.tops_m, lane));
     int cnt = 0;
     constexpr int kBatch = 8;  // loads in flight per lane before any is used
     for (int i0 = 0; i0 < m; i0 += 32 * kBatch) {

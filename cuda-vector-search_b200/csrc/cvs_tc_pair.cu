@@ -48,17 +48,19 @@ struct PairLayout {
   int stage_bytes;
   int bars;
   int hist;
+  int scratch;
   int total;
 };
 
-__host__ __device__ constexpr PairLayout pair_layout(bool qres, int ksl, int subs) {
+__host__ __device__ constexpr PairLayout pair_layout(bool qres, int ksl, int subs, int scratch_keys) {
   PairLayout l{};
   l.stage_bytes = qres ? kXHalf : (kXHalf + kQSlice);
   l.stages = qres ? ksl * kQSlice : 0;
   l.bars = l.stages + kStages * l.stage_bytes;
   // full[6], empty[6], tfull[2], tempty[2], qfull, done; tmem holder, abort
   l.hist = l.bars + 8 * (2 * kStages + 6) + 16;
-  l.total = l.hist + pair_epi_warps(subs) * 256 * 4;
+  l.scratch = l.hist + pair_epi_warps(subs) * 256 * 4;
+  l.total = l.scratch + pair_epi_warps(subs) * scratch_keys * 8;
   return l;
 }
 
@@ -82,6 +84,9 @@ struct PairShared {
     return reinterpret_cast<volatile int*>(base + l.bars + 8 * (2 * kStages + 6) + 4);
   }
   __device__ uint32_t* hist(int w) const { return reinterpret_cast<uint32_t*>(base + l.hist) + 256 * w; }
+  __device__ uint64_t* scratch(int w, int keys) const {
+    return reinterpret_cast<uint64_t*>(base + l.scratch) + static_cast<size_t>(keys) * w;
+  }
 };
 
 template <bool QRES, class Epi>
@@ -93,7 +98,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
   PairShared sh;
   sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
-  sh.l = pair_layout(QRES, a.ksl, Epi::kSubs);
+  sh.l = pair_layout(QRES, a.ksl, Epi::kSubs, Epi::kScratchKeys);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -266,7 +271,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
           epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
           if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
             epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a,
-                              sh.hist(ew), lane);
+                              Epi::jrank(a.k, a.segs * Epi::kSubs), sh.hist(ew),
+                              sh.scratch(ew, Epi::kScratchKeys), lane);
           }
         }
       }
@@ -291,7 +297,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
             const int src = __ffs(need) - 1;
             need &= need - 1;
             const int qs = __shfl_sync(kFullMask, q, src);
-            const uint32_t kth = warp_kth_top<kTopsPerLane>(a.tops + static_cast<size_t>(qs) * lists, lists, a.k, lane);
+            const int mneed = (a.k + Epi::jrank(a.k, lists) - 1) / Epi::jrank(a.k, lists);
+            const uint32_t kth = warp_kth_top<kTopsPerLane>(a.tops + static_cast<size_t>(qs) * lists, lists, mneed, lane);
             if (lane == src && kth != 0) {
               atomicMax(a.gthr + qs, kth);
               epi.bound = fmaxf(epi.bound, score_of_bits(kth));
@@ -301,7 +308,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
       }
     }
     if constexpr (!is_store<Epi>::value) {
-      if (ok) epi.finish(a, q, seg * Epi::kSubs + sub, qvalid, sh.hist(ew));
+      if (ok) epi.finish(a, q, seg * Epi::kSubs + sub, qvalid, sh.hist(ew), sh.scratch(ew, Epi::kScratchKeys),
+                          a.segs * Epi::kSubs);
     }
   }
 
@@ -322,7 +330,7 @@ const void* pair_kernel_ptr() {
 template <bool QRES, class Epi>
 cudaError_t pair_launch_one(const CUtensorMap* qmap, const CUtensorMap* xmap, const TcArgs& a,
                             cudaStream_t stream) {
-  const PairLayout l = pair_layout(QRES, a.ksl, Epi::kSubs);
+  const PairLayout l = pair_layout(QRES, a.ksl, Epi::kSubs, Epi::kScratchKeys);
   const size_t smem = static_cast<size_t>(l.total) + 1024;
   auto kern = tc_pair_kernel<QRES, Epi>;
   cudaError_t e =
@@ -335,7 +343,7 @@ cudaError_t pair_launch_one(const CUtensorMap* qmap, const CUtensorMap* xmap, co
 
 template <bool QRES, class Epi>
 int pair_clusters_one(int ksl) {
-  const PairLayout l = pair_layout(QRES, ksl, Epi::kSubs);
+  const PairLayout l = pair_layout(QRES, ksl, Epi::kSubs, Epi::kScratchKeys);
   const size_t smem = static_cast<size_t>(l.total) + 1024;
   auto kern = tc_pair_kernel<QRES, Epi>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
@@ -384,8 +392,10 @@ int pair_clusters_epi(int epi, int ksl) {
 
 }  // namespace
 
-bool tc_pair_resident_queries(int ksl) {
-  return static_cast<size_t>(pair_layout(true, ksl, 2).total) + 1024 <= 232448;
+bool tc_pair_resident_queries(int epi, int ksl) {
+  const int subs = epi == kEpiTopkBuf ? EpiTopkBuf::kSubs : 2;
+  const int scratch = epi == kEpiTopkBuf ? EpiTopkBuf::kScratchKeys : 0;
+  return static_cast<size_t>(pair_layout(true, ksl, subs, scratch).total) + 1024 <= 232448;
 }
 
 int tc_pair_max_clusters(int epi, bool resident_queries, int ksl) {
@@ -394,7 +404,7 @@ int tc_pair_max_clusters(int epi, bool resident_queries, int ksl) {
 
 cudaError_t tc_pair_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                            const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream) {
-  if (resident_queries && !tc_pair_resident_queries(a.ksl)) return cudaErrorInvalidValue;
+  if (resident_queries && !tc_pair_resident_queries(epi, a.ksl)) return cudaErrorInvalidValue;
   return resident_queries ? pair_launch_epi<true>(epi, qmap, xmap, a, stream)
                           : pair_launch_epi<false>(epi, qmap, xmap, a, stream);
 }

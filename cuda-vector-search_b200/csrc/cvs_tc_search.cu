@@ -48,10 +48,11 @@ struct Layout {
   int stage_bytes;
   int bars;       // mbarriers
   int hist;       // per epilogue warp radix histograms
+  int scratch;    // per epilogue warp compaction buffers (buffer epilogue)
   int total;
 };
 
-__host__ __device__ constexpr Layout make_layout(bool qres, int ksl, int subs) {
+__host__ __device__ constexpr Layout make_layout(bool qres, int ksl, int subs, int scratch_keys) {
   Layout l{};
   l.q_res = 0;
   l.stage_bytes = qres ? kXSliceBytes : (kXSliceBytes + kQSliceBytes);
@@ -59,7 +60,8 @@ __host__ __device__ constexpr Layout make_layout(bool qres, int ksl, int subs) {
   l.bars = l.stages + num_stages(qres) * l.stage_bytes;
   // full[4], empty[4], tfull[2], tempty[2], qfull, done, tmem holder, abort
   l.hist = l.bars + 8 * (2 * kTcStages + 6) + 16;
-  l.total = l.hist + epi_warps(subs) * 256 * 4;
+  l.scratch = l.hist + epi_warps(subs) * 256 * 4;
+  l.total = l.scratch + epi_warps(subs) * scratch_keys * 8;
   return l;
 }
 
@@ -87,6 +89,9 @@ struct Shared {
   __device__ uint32_t* hist(int w) const {
     return reinterpret_cast<uint32_t*>(base + l.hist) + 256 * w;
   }
+  __device__ uint64_t* scratch(int w, int keys) const {
+    return reinterpret_cast<uint64_t*>(base + l.scratch) + static_cast<size_t>(keys) * w;
+  }
 };
 
 // ---------------------------------------------------------------------------
@@ -101,7 +106,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
   Shared sh;
   sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
-  sh.l = make_layout(QRES, a.ksl, Epi::kSubs);
+  sh.l = make_layout(QRES, a.ksl, Epi::kSubs, Epi::kScratchKeys);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -257,8 +262,9 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         } else {
           epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
           if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
-            epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a, sh.hist(ew),
-                              lane);
+            epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a,
+                              Epi::jrank(a.k, a.segs * Epi::kSubs), sh.hist(ew),
+                              sh.scratch(ew, Epi::kScratchKeys), lane);
           }
         }
       }
@@ -280,7 +286,8 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
             const int src = __ffs(need) - 1;
             need &= need - 1;
             const int qs = __shfl_sync(kFullMask, q, src);
-            const uint32_t kth = warp_kth_top<kTopsPerLane>(a.tops + static_cast<size_t>(qs) * lists, lists, a.k, lane);
+            const int mneed = (a.k + Epi::jrank(a.k, lists) - 1) / Epi::jrank(a.k, lists);
+            const uint32_t kth = warp_kth_top<kTopsPerLane>(a.tops + static_cast<size_t>(qs) * lists, lists, mneed, lane);
             if (lane == src && kth != 0) {
               atomicMax(a.gthr + qs, kth);
               epi.bound = fmaxf(epi.bound, score_of_bits(kth));
@@ -290,7 +297,8 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
       }
     }
     if constexpr (!is_store<Epi>::value) {
-      if (ok) epi.finish(a, q, seg * Epi::kSubs + sub, qvalid, sh.hist(ew));
+      if (ok) epi.finish(a, q, seg * Epi::kSubs + sub, qvalid, sh.hist(ew), sh.scratch(ew, Epi::kScratchKeys),
+                          a.segs * Epi::kSubs);
     }
   }
 
@@ -305,7 +313,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
 template <bool QRES, class Epi>
 cudaError_t launch_one(const CUtensorMap* qmap, const CUtensorMap* xmap, const TcArgs& a,
                        cudaStream_t stream) {
-  const Layout l = make_layout(QRES, a.ksl, Epi::kSubs);
+  const Layout l = make_layout(QRES, a.ksl, Epi::kSubs, Epi::kScratchKeys);
   const size_t smem = static_cast<size_t>(l.total) + 1024;
   auto kern = tc_search_kernel<QRES, Epi>;
   cudaError_t e =
@@ -331,6 +339,13 @@ cudaError_t launch_epi(int epi, const CUtensorMap* qmap, const CUtensorMap* xmap
 
 }  // namespace
 
+bool tc_resident_queries(int epi, int ksl) {
+  if (ksl > kTcMaxResidentSlices) return false;
+  const int subs = epi == kEpiTopkBuf ? EpiTopkBuf::kSubs : 2;
+  const int scratch = epi == kEpiTopkBuf ? EpiTopkBuf::kScratchKeys : 0;
+  return static_cast<size_t>(make_layout(true, ksl, subs, scratch).total) + 1024 <= 232448;
+}
+
 int tc_lists_per_segment(int epi) {
   switch (epi) {
     case kEpiTopkReg16: return EpiTopkReg<16>::kSubs;
@@ -342,7 +357,7 @@ int tc_lists_per_segment(int epi) {
 
 cudaError_t tc_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                       const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream) {
-  if (resident_queries && a.ksl > kTcMaxResidentSlices) return cudaErrorInvalidValue;
+  if (resident_queries && !tc_resident_queries(epi, a.ksl)) return cudaErrorInvalidValue;
   return resident_queries ? launch_epi<true>(epi, qmap, xmap, a, stream)
                           : launch_epi<false>(epi, qmap, xmap, a, stream);
 }
