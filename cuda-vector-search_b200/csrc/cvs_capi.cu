@@ -131,7 +131,8 @@ struct Plan {
   int qtiles = 0, segs = 0, tiles_per_seg = 0, ntiles = 0;
   int cap = 0;
   int lists = 0;  // candidate lists per query (segments x lists per segment)
-  size_t bound_bytes = 0;  // per-query shared bounds at the start of the workspace
+  size_t bound_bytes = 0;  // per-query bounds, per-list tops and counts at the start of the workspace
+  size_t clear_bytes = 0;  // the part of it cleared per call
   int rows_per_seg = 0;
   size_t ws_bytes = 0;
 };
@@ -195,7 +196,8 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->segs = static_cast<int>((n + p->rows_per_seg - 1) / p->rows_per_seg);
     p->cap = k;
     p->lists = p->segs;
-    p->bound_bytes = round_up(static_cast<size_t>(b) * 4 * (1 + p->lists), kWsAlign);
+    p->clear_bytes = static_cast<size_t>(b) * 4 * (1 + p->lists);
+    p->bound_bytes = round_up(p->clear_bytes, kWsAlign);
     p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
     return CVS_OK;
   }
@@ -212,8 +214,11 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
   }
   plan_tc_grid(p, b, n, dev.sms, chunks, p->epi, d_pad, bq);
   p->lists = p->segs * tc_lists_per_segment(p->epi);
-  // Per-query shared bound and per-list best scores, both cleared per call.
-  p->bound_bytes = round_up(static_cast<size_t>(b) * 4 * (1 + p->lists), kWsAlign);
+  // Per-query shared bound, per-list published scores and (buffer lists) per-list
+  // key counts, all cleared per call.
+  const bool counted = p->epi == kEpiTopkBuf;
+  p->clear_bytes = static_cast<size_t>(b) * 4 * (1 + p->lists * (counted ? 2 : 1));
+  p->bound_bytes = round_up(p->clear_bytes, kWsAlign);
   p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
   return CVS_OK;
 }
@@ -296,8 +301,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   const bool prof = g_prof_start && g_prof_stop;
   cudaError_t e;
   // The shared per-query bounds must start at "none" (0) on every call.
-  const size_t clear_bytes = static_cast<size_t>(b) * 4 * (1 + p.lists);
-  if (p.bound_bytes && (e = cudaMemsetAsync(bounds, 0, clear_bytes, s)) != cudaSuccess)
+  if (p.clear_bytes && (e = cudaMemsetAsync(bounds, 0, p.clear_bytes, s)) != cudaSuccess)
     return cuda_fail(e, "clearing the per-query bounds");
   if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   if (p.gemv) {
@@ -333,6 +337,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     a.part = part;
     a.gthr = bounds;
     a.tops = bounds + b;
+    a.counts = p.epi == kEpiTopkBuf ? reinterpret_cast<int*>(bounds + b + static_cast<size_t>(b) * p.lists) : nullptr;
     a.err = dev.err;
     e = p.pair ? tc_pair_launch(p.epi, p.qres, &qmap, &xmap, a, s) : tc_launch(p.epi, p.qres, &qmap, &xmap, a, s);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 search launch");
@@ -344,11 +349,13 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   m.lists = p.lists;
   m.stride = p.cap;
   m.per_list = k;
+  // Buffer lists end with up to cap keys each; their counts follow the tops.
+  m.counts = (!p.gemv && p.epi == kEpiTopkBuf)
+                 ? reinterpret_cast<const int*>(bounds + b + static_cast<size_t>(b) * p.lists)
+                 : nullptr;
   m.k = k;
   m.id_offset = id_offset;
   m.bounds = bounds;
-  // Register top-k lists and GEMV CTAs publish their best scores; the buffer
-  // epilogue does not.
   m.tops = bounds + b;
   m.tops_n = p.lists;
   // Register lists and GEMV CTAs publish their best score (m = k lists needed);
@@ -520,6 +527,26 @@ extern "C" cvs_status cvs_fused_topk_noalloc(const void* q_f16, int64_t b, const
   if ((st = device_info(&dev)) != CVS_OK) return st;
   Plan p;
   if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p)) != CVS_OK) return st;
+  if (p.ws_bytes > kNoAllocScratchBytes && plan_chunks == 0) {
+    // Automatic plan too large: the most corpus segments whose candidate lists
+    // fit (list bytes grow with the segment count).
+    int lo = 1, hi = p.segs - 1, best = 0;
+    while (lo <= hi) {
+      const int mid = (lo + hi) / 2;
+      Plan t;
+      if ((st = plan_fused(b, n, d_pad, k, mid, dev, &t)) != CVS_OK) return st;
+      if (t.ws_bytes <= kNoAllocScratchBytes) {
+        best = mid;
+        lo = mid + 1;
+      } else {
+        hi = mid - 1;
+      }
+    }
+    if (best > 0) {
+      plan_chunks = best;
+      if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p)) != CVS_OK) return st;
+    }
+  }
   if (p.ws_bytes > kNoAllocScratchBytes)
     return fail(CVS_ERR_WORKSPACE,
                 "this search needs %zu bytes of scratch but the built-in scratch holds %zu "

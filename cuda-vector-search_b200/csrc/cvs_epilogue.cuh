@@ -37,9 +37,9 @@ __device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
 }
 
 // Rounds at which a query's bound is recomputed from the lists' published
-// maxima: after tiles 1..7, then after every fourth tile. In each round one
+// values: after tiles 0..7, then after every fourth tile. In each round one
 // list per query (a rotating choice, spreading the work over the CTAs) does it.
-__device__ __forceinline__ bool tops_round(int t) { return t >= 1 && (t < 8 || (t & 3) == 3); }
+__device__ __forceinline__ bool tops_round(int t) { return t < 8 || (t & 3) == 3; }
 
 __device__ __forceinline__ bool tops_refresher(int q, int t, int list, int lists) {
   return static_cast<int>((static_cast<unsigned>(q) * 2654435761u + static_cast<unsigned>(t) * 40503u) %
@@ -189,9 +189,6 @@ struct EpiTopkReg {
   }
 };
 
-// Per-query candidate buffer of `cap` keys in global memory (L2 resident).
-// A key is appended when its score beats the current k-th best; when a list
-// could overflow on the next chunk, the warp cooperatively keeps its top k.
 // Rank of the per-list value a list publishes (its J-th best) and how many lists
 // must reach a value for it to bound the query's k-th best (m lists x J rows
 // >= k rows). With at least 2k lists this is (1, k): every list publishes its
@@ -212,26 +209,51 @@ __host__ __device__ __forceinline__ int tops_m(int k, int lists) {
 // trip, radix-selects its top k and J-th best there, writes the top k back and
 // publishes the J-th best for the query's bound.
 struct EpiTopkBuf {
-  static constexpr int kSubs = 1;
+  // Two column stripes per TMEM quadrant, as the register lists.
+  static constexpr int kSubs = 2;
   static constexpr bool kTops = true;
   static constexpr int kScratchKeys = 512;  // shared-memory compaction up to cap 512 (k <= 256)
+  static constexpr int kRegJ = 4;           // J-th best tracked in registers for J <= kRegJ
   static __device__ __forceinline__ int jrank(int k, int lists) { return tops_j(k, lists); }
   uint64_t* list;
   int cnt;
+  int jr;           // J: rank of the value this list publishes
   float thr;        // k-th best at the last compaction
   float bound;      // shared lower bound of the query (refreshed per tile)
-  float best;       // value this list publishes: its J-th best at the last compaction
+  float best;       // value this list publishes: a lower bound on its J-th best
+  float tj[kRegJ];  // best kRegJ scores appended so far, descending
   uint32_t published;
   uint32_t top_published;
 
-  __device__ __forceinline__ void init(const TcArgs&) {
+  __device__ __forceinline__ void init(const TcArgs& a) {
     list = nullptr;
     cnt = 0;
+    jr = tops_j(a.k, a.segs * kSubs);
     thr = -INFINITY;
     bound = -INFINITY;
     best = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kRegJ; ++i) tj[i] = -INFINITY;
     published = 0;
     top_published = 0;
+  }
+
+  // Keeps tj the kRegJ largest appended scores (compare-exchange chain).
+  __device__ __forceinline__ void track(float s) {
+#pragma unroll
+    for (int i = 0; i < kRegJ; ++i) {
+      const float hi = fmaxf(tj[i], s);
+      s = fminf(tj[i], s);
+      tj[i] = hi;
+    }
+  }
+
+  // tj[jr - 1] without a run-time register index.
+  __device__ __forceinline__ float reg_jth() const {
+    float v = tj[0];
+#pragma unroll
+    for (int i = 1; i < kRegJ; ++i) v = jr > i ? tj[i] : v;
+    return v;
   }
 
   // Keeps the top min(k, m) keys of lane src's list and records its k-th best
@@ -264,12 +286,12 @@ struct EpiTopkBuf {
           base += __popc(bal);
         }
       }
-      if (m >= jrank) jth = warp_kth_key(ContigKeys{scratch}, m, jrank, hist, lane);
+      if (jrank > kRegJ && m >= jrank) jth = warp_kth_key(ContigKeys{scratch}, m, jrank, hist, lane);
       __syncwarp();
     } else {
       kth = warp_kth_key(ContigKeys{L}, m, a.k, hist, lane);
       warp_compact_ge(L, m, kth, lane);
-      jth = warp_kth_key(ContigKeys{L}, a.k, jrank, hist, lane);
+      if (jrank > kRegJ) jth = warp_kth_key(ContigKeys{L}, a.k, jrank, hist, lane);
     }
     if (lane == src) {
       if (m > a.k) {
@@ -297,12 +319,17 @@ struct EpiTopkBuf {
       while (m) {
         const int j = __ffs(m) - 1;
         m &= m - 1;
-        list[cnt++] = make_key(pick(r, j), static_cast<uint32_t>(row0 + j));
+        const float s = pick(r, j);
+        list[cnt++] = make_key(s, static_cast<uint32_t>(row0 + j));
+        track(s);
       }
     }
   }
 
+  // The list holds at least J rows scoring >= best; m = ceil(k / J) lists
+  // reaching a value v therefore prove k rows >= v.
   __device__ __forceinline__ void publish_top(const TcArgs& a, int q, int list_idx, int lists) {
+    if (jr <= kRegJ) best = fmaxf(best, reg_jth());
     if (best == -INFINITY) return;
     const uint32_t o = ordered_bits(best);
     if (o > top_published) {
@@ -313,14 +340,16 @@ struct EpiTopkBuf {
     }
   }
 
+  // The list stays as it is (at most cap keys, unsorted); the merge reads
+  // counts[q][list] keys of it. Lists whose J is beyond the register range
+  // compact once more so that their J-th best can be published.
   __device__ __forceinline__ void finish(const TcArgs& a, int q, int list_idx, bool qvalid, uint32_t* hist,
                                          uint64_t* scratch, int lists) {
     const int lane = threadIdx.x & 31;
-    const int jrank = tops_j(a.k, lists);
-    compact_lanes(__ballot_sync(kFullMask, qvalid && (cnt > a.k || cnt >= jrank)), a, jrank, hist, scratch,
-                  lane);
+    if (jr > kRegJ)
+      compact_lanes(__ballot_sync(kFullMask, qvalid && cnt >= jr), a, jr, hist, scratch, lane);
     if (qvalid) {
-      for (int j = cnt; j < a.k; ++j) list[j] = 0ull;
+      a.counts[static_cast<size_t>(q) * lists + list_idx] = cnt;
       publish_top(a, q, list_idx, lists);
     }
   }

@@ -39,7 +39,8 @@ struct TcArgs {
   int cap;            // slots per candidate list; cap >= k
   uint64_t* part;     // [b][segs * lists per segment][cap] ordered keys
   uint32_t* gthr;     // [b] shared per-query lower bounds (ordered bits), zeroed per call
-  uint32_t* tops;     // [b][segs * lists per segment] each list's best score (ordered bits), zeroed per call
+  uint32_t* tops;     // [b][segs * lists per segment] each list's published score (ordered bits), zeroed per call
+  int* counts;        // [b][segs * lists per segment] keys each buffer list ends with (buffer epilogue)
   void* scores_out;   // [b][n] fp32/fp16 for the store epilogues
   int* err;           // device error word
 };
@@ -86,6 +87,7 @@ int gemv_blocks_per_sm(int b, int d_pad);
 // ---- merge of per-segment candidate lists into the final sorted top-k ------
 struct MergeKeysArgs {
   const uint64_t* part;  // [b][lists][stride], first per_list entries of each used
+  const int* counts;     // [b][lists] entries used per list (then per_list is ignored) or null
   int b;
   int lists;
   int stride;

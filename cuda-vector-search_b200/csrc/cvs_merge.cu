@@ -19,23 +19,37 @@ namespace cvs {
 
 namespace {
 
-constexpr int kMergeWarps = 2;
+constexpr int kMergeWarps = 2;       // queries per CTA of the list merge
 constexpr int kMergeMaxK = 1024;
-constexpr int kSurvivorCap = 512;
+constexpr int kKeysThreads = 256;     // one CTA (8 warps) per query in the key merge
+constexpr int kKeysWarps = kKeysThreads / 32;
+constexpr int kKeysBatch = 16;        // 32-key rows in flight per warp
 constexpr int kMergeTopsPerLane = 16;  // up to 512 lists per query
 
-// Shared memory per warp: radix histogram, k selected keys, survivor buffer.
+// Shared memory per warp of the list merge: radix histogram, k selected keys.
 __host__ __device__ constexpr size_t merge_warp_bytes(int k) {
-  return 256 * 4 + static_cast<size_t>(k) * 8 + static_cast<size_t>(kSurvivorCap) * 8;
+  return 256 * 4 + static_cast<size_t>(k) * 8;
 }
 
+// Survivors of the bound filter kept in shared memory (4k, at least 512).
+__host__ __device__ constexpr int survivor_cap(int k) { return 4 * k > 512 ? 4 * k : 512; }
+// Key-merge CTA: histogram, k selected keys, survivors, two counters and the bound.
+__host__ __device__ constexpr size_t keys_smem(int k) {
+  return 256 * 4 + static_cast<size_t>(k) * 8 + static_cast<size_t>(survivor_cap(k)) * 8 + 16;
+}
+
+// Keys of one query: `lists` lists of `stride` slots, of which the first
+// min(count, stride) hold keys (count = counts[list], or per_list for all).
 struct PartKeys {
   const uint64_t* p;  // this query's [lists][stride] block
+  const int* counts;  // this query's [lists] counts or null
   int stride;
   int per_list;
   __device__ __forceinline__ uint64_t operator()(int i) const {
-    if (stride == per_list) return p[i];
-    return p[static_cast<size_t>(i / per_list) * stride + (i % per_list)];
+    const int l = i / stride;
+    const int j = i - l * stride;
+    const int used = counts ? min(counts[l], stride) : per_list;
+    return j < used ? p[i] : 0ull;
   }
 };
 
@@ -53,8 +67,19 @@ struct ListKeys {
   }
 };
 
-// Selects the k best keys of acc(0..m) and writes them in rank order. Empty
-// keys (0) fill the tail when fewer than k real candidates exist.
+__device__ __forceinline__ void emit_key(uint64_t key, int rank, long long id_offset, float* out_v,
+                                         long long* out_i) {
+  if (key == 0ull) {
+    out_v[rank] = -INFINITY;
+    out_i[rank] = -1;
+  } else {
+    out_v[rank] = key_score(key);
+    out_i[rank] = static_cast<long long>(key_row(key)) + id_offset;
+  }
+}
+
+// One warp: selects the k best keys of acc(0..m) and writes them in rank order.
+// Empty keys (0) fill the tail when fewer than k real candidates exist.
 template <class Acc>
 __device__ void select_and_emit(const Acc& acc, int m, int k, long long id_offset, uint32_t* hist,
                                 uint64_t* sel, float* out_v, long long* out_i, int lane) {
@@ -81,71 +106,129 @@ __device__ void select_and_emit(const Acc& acc, int m, int k, long long id_offse
       const uint64_t o = sel[t];
       rank += (o > key) || (o == key && t < j);
     }
-    if (key == 0ull) {
-      out_v[rank] = -INFINITY;
-      out_i[rank] = -1;
-    } else {
-      out_v[rank] = key_score(key);
-      out_i[rank] = static_cast<long long>(key_row(key)) + id_offset;
-    }
+    emit_key(key, rank, id_offset, out_v, out_i);
   }
   __syncwarp();
 }
 
-// Per query: when the search kernel left a lower bound on the query's k-th best
-// score (a.bounds), one coalesced pass keeps only the keys at or above it --
-// typically a few times k of the lists*k keys -- in shared memory, and the
-// selection runs there. Without a bound, or if more than kSurvivorCap keys
-// survive, the selection runs over all keys.
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_keys_kernel(const MergeKeysArgs a) {
-  extern __shared__ uint8_t smem[];
+// One CTA per query. Warp 0 forms the query's bound: the kernel's running
+// bound (a.bounds) raised to the tops_m-th largest per-list published score.
+// All eight warps then stream the query's lists in 32-key rows (16 rows in
+// flight per warp) and append the keys at or above the bound -- typically one
+// to three times k of them -- to a shared survivor buffer; warp 0 radix-selects
+// the k-th best survivor, the k winners are gathered, and every thread writes
+// some of them straight to their output rank (the number of larger winners).
+// If more survivors than the buffer holds appear (no bound, or a weak one),
+// warp 0 selects over all keys instead.
+__global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKeysArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q = blockIdx.x * kMergeWarps + warp;
-  uint8_t* mine = smem + static_cast<size_t>(warp) * merge_warp_bytes(a.k);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(mine);
-  uint64_t* sel = reinterpret_cast<uint64_t*>(mine + 256 * 4);
+  const int q = blockIdx.x;
+  const int scap = survivor_cap(a.k);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem);
+  uint64_t* sel = reinterpret_cast<uint64_t*>(smem + 256 * 4);
   uint64_t* surv = sel + a.k;
-  if (q >= a.b) return;  // whole warp
-  const PartKeys acc{a.part + static_cast<size_t>(q) * a.lists * a.stride, a.stride, a.per_list};
-  const int m = a.lists * a.per_list;
+  int* s_cnt = reinterpret_cast<int*>(surv + scap);  // [0] survivors, [1] winners
+  uint32_t* s_bound = reinterpret_cast<uint32_t*>(s_cnt + 2);
+  const uint64_t* base = a.part + static_cast<size_t>(q) * a.lists * a.stride;
+  const int* counts = a.counts ? a.counts + static_cast<size_t>(q) * a.lists : nullptr;
   float* out_v = a.out_v + static_cast<size_t>(q) * a.k;
   long long* out_i = a.out_i + static_cast<size_t>(q) * a.k;
-  if (a.bounds != nullptr) {
-    uint32_t bound;
-    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(bound) : "l"(a.bounds + q));
-    // The k-th largest of the lists' final best scores is usually a much
-    // tighter bound than the kernel's running one.
-    if (a.tops != nullptr && a.tops_n <= 32 * kMergeTopsPerLane)
-      bound = max(bound, warp_kth_top<kMergeTopsPerLane>(a.tops + static_cast<size_t>(q) * a.tops_n,
-                                                         a.tops_n, a.tops_m, lane));
-    int cnt = 0;
-    constexpr int kBatch = 8;  // loads in flight per lane before any is used
-    for (int i0 = 0; i0 < m; i0 += 32 * kBatch) {
-      uint64_t keys[kBatch];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i = i0 + 32 * u + lane;
-        keys[u] = i < m ? acc(i) : 0ull;
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const bool keep = keys[u] != 0ull && static_cast<uint32_t>(keys[u] >> 32) >= bound;
-        const unsigned bal = __ballot_sync(kFullMask, keep);
-        if (keep) {
-          const int pos = cnt + __popc(bal & ((1u << lane) - 1u));
-          if (pos < kSurvivorCap) surv[pos] = keys[u];
-        }
-        cnt += __popc(bal);
-      }
+
+  if (warp == 0) {
+    uint32_t bound = 0;
+    if (a.bounds != nullptr) {
+      asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(bound) : "l"(a.bounds + q));
+      if (a.tops != nullptr && a.tops_n <= 32 * kMergeTopsPerLane)
+        bound = max(bound, warp_kth_top<kMergeTopsPerLane>(a.tops + static_cast<size_t>(q) * a.tops_n,
+                                                           a.tops_n, a.tops_m, lane));
     }
-    __syncwarp();
-    if (cnt <= kSurvivorCap) {
-      select_and_emit(ContigKeys{surv}, cnt, a.k, a.id_offset, hist, sel, out_v, out_i, lane);
-      return;
+    if (lane == 0) {
+      *s_bound = bound;
+      s_cnt[0] = 0;
+      s_cnt[1] = 0;
     }
   }
-  select_and_emit(acc, m, a.k, a.id_offset, hist, sel, out_v, out_i, lane);
+  __syncthreads();
+  const uint32_t bound = *s_bound;
+  const PartKeys all{base, counts, a.stride, a.per_list};
+  const int m = a.lists * a.stride;
+  if (bound == 0) {  // nothing to filter with
+    if (warp == 0) select_and_emit(all, m, a.k, a.id_offset, hist, sel, out_v, out_i, lane);
+    return;
+  }
+
+  // Rows of 32 slots: counted lists are walked list by list (row r of list l
+  // covers slots 32r..32r+31), uniform lists as one contiguous run.
+  const int L = counts ? a.lists : 1;
+  const int S = counts ? a.stride : a.lists * a.per_list;
+  const int R = (S + 31) / 32;
+  const int rows = L * R;
+  for (int r0 = warp * kKeysBatch; r0 < rows; r0 += kKeysWarps * kKeysBatch) {
+    uint64_t keys[kKeysBatch];
+#pragma unroll
+    for (int u = 0; u < kKeysBatch; ++u) {
+      const int row = r0 + u;
+      keys[u] = 0ull;
+      if (row < rows) {
+        const int l = row / R;
+        const int j = (row - l * R) * 32 + lane;
+        const int used = counts ? min(counts[l], S) : S;
+        if (j < used) keys[u] = base[static_cast<size_t>(l) * S + j];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kKeysBatch; ++u) {
+      const bool keep = keys[u] != 0ull && static_cast<uint32_t>(keys[u] >> 32) >= bound;
+      const unsigned bal = __ballot_sync(kFullMask, keep);
+      if (bal) {
+        int pos = 0;
+        if (lane == __ffs(bal) - 1) pos = atomicAdd(s_cnt, __popc(bal));
+        pos = __shfl_sync(kFullMask, pos, __ffs(bal) - 1) + __popc(bal & ((1u << lane) - 1u));
+        if (keep && pos < scap) surv[pos] = keys[u];
+      }
+    }
+  }
+  __syncthreads();
+  const int cnt = s_cnt[0];
+  if (cnt > scap) {
+    if (warp == 0) select_and_emit(all, m, a.k, a.id_offset, hist, sel, out_v, out_i, lane);
+    return;
+  }
+  // k-th best survivor (warp 0), then the winners (keys are unique, so exactly
+  // min(k, cnt) survivors are >= it).
+  if (warp == 0) {
+    const uint64_t kth = cnt > a.k ? warp_kth_key(ContigKeys{surv}, cnt, a.k, hist, lane) : 0ull;
+    if (lane == 0) *reinterpret_cast<uint64_t*>(hist) = kth;
+  }
+  __syncthreads();
+  const uint64_t kth = *reinterpret_cast<const uint64_t*>(hist);
+  for (int i0 = warp * 32; i0 < cnt; i0 += kKeysThreads) {
+    const int i = i0 + lane;
+    const uint64_t key = i < cnt ? surv[i] : 0ull;
+    const bool take = i < cnt && key >= kth;
+    const unsigned bal = __ballot_sync(kFullMask, take);
+    if (bal) {
+      int pos = 0;
+      if (lane == __ffs(bal) - 1) pos = atomicAdd(s_cnt + 1, __popc(bal));
+      pos = __shfl_sync(kFullMask, pos, __ffs(bal) - 1) + __popc(bal & ((1u << lane) - 1u));
+      if (take && pos < a.k) sel[pos] = key;
+    }
+  }
+  __syncthreads();
+  const int won = min(s_cnt[1], a.k);
+  for (int j = won + threadIdx.x; j < a.k; j += kKeysThreads) sel[j] = 0ull;
+  __syncthreads();
+  for (int j = threadIdx.x; j < a.k; j += kKeysThreads) {
+    const uint64_t key = sel[j];
+    int rank = 0;
+    for (int t = 0; t < a.k; ++t) {
+      const uint64_t o = sel[t];
+      rank += (o > key) || (o == key && t < j);
+    }
+    emit_key(key, rank, a.id_offset, out_v, out_i);
+  }
 }
 
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const MergeListsArgs a) {
@@ -167,13 +250,14 @@ size_t merge_smem(int k) { return kMergeWarps * merge_warp_bytes(k); }
 }  // namespace
 
 cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream) {
-  if (a.k < 1 || a.k > kMergeMaxK || a.b < 1) return cudaErrorInvalidValue;
-  const size_t smem = merge_smem(a.k);
+  if (a.k < 1 || a.k > kMergeMaxK || a.b < 1 || a.stride < 1) return cudaErrorInvalidValue;
+  // Lists without counts must be packed (the filter walks them as one run).
+  if (!a.counts && a.per_list != a.stride) return cudaErrorInvalidValue;
+  const size_t smem = keys_smem(a.k);
   cudaError_t e = cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const unsigned grid = static_cast<unsigned>((a.b + kMergeWarps - 1) / kMergeWarps);
-  merge_keys_kernel<<<grid, kMergeWarps * 32, smem, stream>>>(a);
+  merge_keys_kernel<<<static_cast<unsigned>(a.b), kKeysThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -37,7 +37,10 @@ namespace {
 constexpr int kRows = kTcN / 2;                  // corpus rows per CTA per tile
 constexpr int kQSlice = kTcM * kTcK * 2;         // 16 KB: 128 queries x 64 halves
 constexpr int kXHalf = kRows * kTcK * 2;         // 16 KB: 128 corpus rows x 64 halves
-constexpr int kStages = 6;
+constexpr int kStages = 6;  // barrier arrays are sized for this many stages
+// Ring depth: 6 stages, or 5 when the epilogue needs shared-memory compaction
+// buffers (8 warps x 4 KB).
+__host__ __device__ constexpr int pair_stages(int scratch_keys) { return scratch_keys > 0 ? 5 : kStages; }
 constexpr uint32_t kTmemCols = 512;
 
 __host__ __device__ constexpr int pair_epi_warps(int subs) { return 4 * subs; }
@@ -56,7 +59,7 @@ __host__ __device__ constexpr PairLayout pair_layout(bool qres, int ksl, int sub
   PairLayout l{};
   l.stage_bytes = qres ? kXHalf : (kXHalf + kQSlice);
   l.stages = qres ? ksl * kQSlice : 0;
-  l.bars = l.stages + kStages * l.stage_bytes;
+  l.bars = l.stages + pair_stages(scratch_keys) * l.stage_bytes;
   // full[6], empty[6], tfull[2], tempty[2], qfull, done; tmem holder, abort
   l.hist = l.bars + 8 * (2 * kStages + 6) + 16;
   l.scratch = l.hist + pair_epi_warps(subs) * 256 * 4;
@@ -94,6 +97,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
     tc_pair_kernel(const __grid_constant__ CUtensorMap qmap,
                    const __grid_constant__ CUtensorMap xmap, const TcArgs a) {
   constexpr int kEpiWarps = pair_epi_warps(Epi::kSubs);
+  constexpr int kS = pair_stages(Epi::kScratchKeys);  // ring depth
   extern __shared__ uint8_t smem_raw[];
   PairShared sh;
   sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -162,8 +166,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
       for (int t = 0; t < ntl && ok; ++t) {
         const int row0 = (t_begin + t) * kTcN + static_cast<int>(rank) * kRows;
         for (int ks = 0; ks < a.ksl; ++ks, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+          const int s = it % kS;
+          const uint32_t ph = (it / kS) & 1;
           if (!mbar_wait(sh.empty(s), ph ^ 1, abort, a.err, 11)) {
             ok = false;
             break;
@@ -177,8 +181,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
         // Leaving early: the even CTA's barriers count both CTAs' copies, so
         // waiting (bounded) on the phases it armed lets the pair's copies land;
         // the odd CTA stays resident until the final cluster barrier.
-        for (int j = max(0, it - kStages); j < it; ++j)
-          mbar_wait_drain(sh.full(j % kStages), (j / kStages) & 1);
+        for (int j = max(0, it - kS); j < it; ++j)
+          mbar_wait_drain(sh.full(j % kS), (j / kS) & 1);
         if (QRES) mbar_wait_drain(sh.qfull(), 0);
       }
     }
@@ -201,8 +205,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTcN);
           for (int ks = 0; ks < a.ksl; ++ks, ++it) {
-            const int s = it % kStages;
-            const uint32_t ph = (it / kStages) & 1;
+            const int s = it % kS;
+            const uint32_t ph = (it / kS) & 1;
             if (!mbar_wait(sh.full(s), ph, abort, a.err, 14)) {
               ok = false;
               break;
@@ -241,7 +245,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
     Epi epi;
     epi.init(a);
     if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
-      if (qvalid) epi.list = a.part + (static_cast<size_t>(q) * a.segs + seg) * a.cap;
+      if (qvalid)
+        epi.list = a.part + (static_cast<size_t>(q) * a.segs * Epi::kSubs + seg * Epi::kSubs + sub) * a.cap;
     }
     bool ok = true;
     for (int t = 0; t < ntl; ++t) {

@@ -38,8 +38,11 @@ __host__ __device__ constexpr int epi_warps(int subs) { return 4 * subs; }
 __host__ __device__ constexpr int tc_threads(int subs) { return 64 + 32 * epi_warps(subs); }
 
 // Resident queries leave room for 3 corpus stages (96 KB in flight, enough to
-// cover HBM latency); streamed queries use 4 stages of 48 KB.
-__host__ __device__ constexpr int num_stages(bool qres) { return qres ? 3 : 4; }
+// cover HBM latency); streamed queries use 4 stages of 48 KB, or 3 when the
+// epilogue needs shared-memory compaction buffers.
+__host__ __device__ constexpr int num_stages(bool qres, int scratch_keys) {
+  return (qres || scratch_keys > 0) ? 3 : 4;
+}
 
 // Shared-memory carve-up (offsets from a 1024-byte aligned base).
 struct Layout {
@@ -57,7 +60,7 @@ __host__ __device__ constexpr Layout make_layout(bool qres, int ksl, int subs, i
   l.q_res = 0;
   l.stage_bytes = qres ? kXSliceBytes : (kXSliceBytes + kQSliceBytes);
   l.stages = qres ? ksl * kQSliceBytes : 0;
-  l.bars = l.stages + num_stages(qres) * l.stage_bytes;
+  l.bars = l.stages + num_stages(qres, scratch_keys) * l.stage_bytes;
   // full[4], empty[4], tfull[2], tempty[2], qfull, done, tmem holder, abort
   l.hist = l.bars + 8 * (2 * kTcStages + 6) + 16;
   l.scratch = l.hist + epi_warps(subs) * 256 * 4;
@@ -101,7 +104,7 @@ template <bool QRES, class Epi>
 __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     tc_search_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap xmap, const TcArgs a) {
-  constexpr int kS = num_stages(QRES);  // ring depth (barrier arrays are sized for the max)
+  constexpr int kS = num_stages(QRES, Epi::kScratchKeys);  // ring depth (barrier arrays are sized for the max)
   extern __shared__ uint8_t smem_raw[];
   Shared sh;
   sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -233,7 +236,8 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     Epi epi;
     epi.init(a);
     if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
-      if (qvalid) epi.list = a.part + (static_cast<size_t>(q) * a.segs + seg) * a.cap;  // kSubs == 1
+      if (qvalid)
+        epi.list = a.part + (static_cast<size_t>(q) * a.segs * Epi::kSubs + seg * Epi::kSubs + sub) * a.cap;
     }
     bool ok = true;
     for (int t = 0; t < ntl; ++t) {

@@ -111,9 +111,11 @@ cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t list
  * plugins from calling cudaMalloc, a serving loop that cannot afford
  * cudaMalloc's synchronisation, a language binding without a device
  * allocator). The candidate lists live in a 16 MiB array built into the
- * library (reserved on every GPU that loads it until the process exits); a
- * problem needing more (b * segments * list slots * 8 bytes, as reported by
- * cvs_fused_topk_workspace_size) is rejected with CVS_ERR_WORKSPACE. The first
+ * library (reserved on every GPU that loads it until the process exits). With
+ * plan_chunks = 0 a plan that needs more (b * segments * list slots * 8 bytes,
+ * as reported by cvs_fused_topk_workspace_size) is replaced by one with fewer
+ * corpus segments; a problem that does not fit even with one segment, or an
+ * explicit plan_chunks that does not fit, is rejected with CVS_ERR_WORKSPACE. The first
  * call on a device looks up the array's address (make it before any stream
  * capture). All calls share the array: calls that overlap on the GPU race, so
  * issue them on one stream. Allocates nothing. No counterpart in the reference.

@@ -64,7 +64,10 @@ def _no_alloc(lib, q, x, k, stream):
     return v.cpu(), i.cpu()
 
 
-@pytest.mark.parametrize("n,d,b,k", [(20000, 768, 256, 10), (30000, 384, 40, 100), (20000, 768, 1, 10)])
+# (300000, 64, 256, 256): the automatic plan needs more than the built-in
+# scratch, so the entry point plans fewer corpus segments.
+@pytest.mark.parametrize("n,d,b,k", [(20000, 768, 256, 10), (30000, 384, 40, 100), (20000, 768, 1, 10),
+                                     (300000, 64, 256, 256)])
 def test_no_alloc_matches_workspace_entry_point(n, d, b, k):
     assert torch.cuda.is_available()
     lib = _lib()
@@ -80,12 +83,13 @@ def test_no_alloc_matches_workspace_entry_point(n, d, b, k):
 
 def test_no_alloc_rejects_oversize_problem():
     lib = _lib()
-    x, q = make(300000, 64, 256, seed=1)
+    # Even one corpus segment needs b * 2 lists * 2048 slots * 8 bytes = 32 MiB.
+    x, q = make(20000, 64, 1024, seed=1)
     x, q = x.cuda(), q.cuda()
     b, n = q.shape[0], x.shape[0]
-    v = torch.empty((b, 256), dtype=torch.float32, device="cuda")
-    i = torch.empty((b, 256), dtype=torch.int64, device="cuda")
-    st = lib.cvs_fused_topk_noalloc(q.data_ptr(), b, x.data_ptr(), n, 64, 256, 0, v.data_ptr(), i.data_ptr(), 0,
+    v = torch.empty((b, 1024), dtype=torch.float32, device="cuda")
+    i = torch.empty((b, 1024), dtype=torch.int64, device="cuda")
+    st = lib.cvs_fused_topk_noalloc(q.data_ptr(), b, x.data_ptr(), n, 64, 1024, 0, v.data_ptr(), i.data_ptr(), 0,
                                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == 3  # CVS_ERR_WORKSPACE
     assert b"built-in scratch" in lib.cvs_last_error()
