@@ -210,14 +210,17 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->cap = k;
   } else {
     p->epi = kEpiTopkBuf;
-    p->cap = static_cast<int>(round_up(static_cast<size_t>(std::max(2 * k, k + 32)), 32));
+    // Room for 2k keys, and at least for the first two tiles' 256 columns of a
+    // list (appended before any shared bound exists) plus one chunk, so that
+    // no list compacts in its first two tiles.
+    p->cap = static_cast<int>(round_up(static_cast<size_t>(std::max({2 * k, k + 32, 2 * kTcN / 2 + 64})), 32));
   }
   plan_tc_grid(p, b, n, dev.sms, chunks, p->epi, d_pad, bq);
   p->lists = p->segs * tc_lists_per_segment(p->epi);
-  // Per-query shared bound, per-list published scores and (buffer lists) per-list
-  // key counts, all cleared per call.
+  // Per-query shared bound, per-list published scores, (buffer lists) per-list
+  // key counts and the per-query-tile tile counters, all cleared per call.
   const bool counted = p->epi == kEpiTopkBuf;
-  p->clear_bytes = static_cast<size_t>(b) * 4 * (1 + p->lists * (counted ? 2 : 1));
+  p->clear_bytes = static_cast<size_t>(b) * 4 * (1 + p->lists * (counted ? 2 : 1)) + 4 * static_cast<size_t>(p->qtiles);
   p->bound_bytes = round_up(p->clear_bytes, kWsAlign);
   p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
   return CVS_OK;
@@ -337,7 +340,11 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     a.part = part;
     a.gthr = bounds;
     a.tops = bounds + b;
+    const size_t list_words = static_cast<size_t>(b) * p.lists * (p.epi == kEpiTopkBuf ? 2 : 1);
     a.counts = p.epi == kEpiTopkBuf ? reinterpret_cast<int*>(bounds + b + static_cast<size_t>(b) * p.lists) : nullptr;
+    // Tiles are claimed at run time; a.segs CTAs (pairs) per query tile share them.
+    a.tile_counter = reinterpret_cast<int*>(bounds + b + list_words);
+    a.dry = p.tiles_per_seg >= kDryMinTiles ? kDryTiles : 0;
     a.err = dev.err;
     e = p.pair ? tc_pair_launch(p.epi, p.qres, &qmap, &xmap, a, s) : tc_launch(p.epi, p.qres, &qmap, &xmap, a, s);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 search launch");

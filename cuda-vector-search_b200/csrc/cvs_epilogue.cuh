@@ -38,13 +38,23 @@ __device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
 
 // Rounds at which a query's bound is recomputed from the lists' published
 // values: after tiles 0..7, then after every fourth tile. In each round one
-// list per query (a rotating choice, spreading the work over the CTAs) does it.
+// list per query (a rotating choice, spreading the work over the CTAs) does it,
+// kDryRefreshers lists in dry rounds.
 __device__ __forceinline__ bool tops_round(int t) { return t < 8 || (t & 3) == 3; }
 
-__device__ __forceinline__ bool tops_refresher(int q, int t, int list, int lists) {
-  return static_cast<int>((static_cast<unsigned>(q) * 2654435761u + static_cast<unsigned>(t) * 40503u) %
-                          static_cast<unsigned>(lists)) == list;
+// The r lists h, h+1, ..., h+r-1 (mod lists) refresh query q in round t.
+__device__ __forceinline__ bool tops_refresher(int q, int t, int list, int lists, int r) {
+  const unsigned h = (static_cast<unsigned>(q) * 2654435761u + static_cast<unsigned>(t) * 40503u) %
+                     static_cast<unsigned>(lists);
+  return (static_cast<unsigned>(list) + static_cast<unsigned>(lists) - h) % static_cast<unsigned>(lists) <
+         static_cast<unsigned>(r);
 }
+
+// Refreshers per query in dry rounds: the epilogue idles there (a dry tile
+// costs a few hundred cycles against several thousand of MMA per tile), and the
+// first real tile needs every query's bound in place, so a refresher that runs
+// late on one CTA must not leave its query without one.
+constexpr int kDryRefreshers = 16;
 
 // Shared per-query lower bound: the largest k-th-best score any list of this
 // query has reached (ordered bits, 0 = none yet). Every list of the query --
@@ -66,15 +76,16 @@ __device__ __forceinline__ void publish_bound(uint32_t* p, float kth, uint32_t& 
   }
 }
 
-// Bit j set when score j exceeds thr and is not below the shared bound (only
-// the first nvalid scores count). Four independent OR chains.
-__device__ __forceinline__ uint32_t above_mask(const uint32_t (&r)[32], float thr, float bound,
-                                               int nvalid) {
+// Bit j set when score j is at least lim = max(list threshold, shared bound)
+// (only the first nvalid scores count). Scores equal to the list threshold are
+// kept: a list revisits its first tiles last, so an equal score may belong to a
+// smaller row id and rank higher. Four independent OR chains.
+__device__ __forceinline__ uint32_t above_mask(const uint32_t (&r)[32], float lim, int nvalid) {
   uint32_t m[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float s = __uint_as_float(r[j]);
-    m[j & 3] |= ((s > thr) && (s >= bound) ? 1u : 0u) << j;
+    m[j & 3] |= (s >= lim ? 1u : 0u) << j;
   }
   const uint32_t all = (m[0] | m[1]) | (m[2] | m[3]);
   return nvalid >= 32 ? all : (all & ((1u << nvalid) - 1u));
@@ -94,6 +105,28 @@ __device__ __forceinline__ float pick(const uint32_t (&r)[32], int j) {
 }
 
 constexpr int kTopsPerLane = 10;  // lists per query <= 320 for the in-kernel refresh
+
+// Dry tiles. A list starts empty, so without a shared bound its first tile
+// would send dozens of scores per query through the slow insertion path while
+// the tensor cores wait (two accumulators let the MMA run only one tile ahead).
+// Instead the first kDryTiles tiles a CTA works on are read "dry" -- they only
+// raise the value each list publishes for the query's bound -- and are computed
+// again, for real, after the CTA's last tile, when the bound from every list's
+// first tiles is in place. The host enables them (TcArgs::dry) when a CTA can
+// expect at least kDryMinTiles tiles (the extra MMA work is kDryTiles / tiles);
+// kDryTiles and kDryMinTiles are in cvs_kernels.h.
+
+// Largest of the first nvalid scores.
+__device__ __forceinline__ float max_valid(const uint32_t (&r)[32], int nvalid) {
+  if (nvalid >= 32) return max32(r);
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nvalid) m = fmaxf(m, __uint_as_float(r[j]));
+  return m;
+}
+
+
 
 // Sorted (score desc, row asc) list of KP slots in registers holding the best
 // k <= KP candidates in its LAST k slots; the first KP-k slots are parked at
@@ -166,14 +199,21 @@ struct EpiTopkReg {
                                           bool qvalid, uint32_t*) {
     if (!qvalid) return;
     const float mx = max32(r);
-    if (!(mx > thr && mx >= bound)) return;
-    uint32_t m = above_mask(r, thr, bound, nvalid);
+    const float lim = fmaxf(thr, bound);
+    if (!(mx >= lim)) return;
+    uint32_t m = above_mask(r, lim, nvalid);
     while (m) {
       const int j = __ffs(m) - 1;
       m &= m - 1;
       const float s = pick(r, j);
-      if (s > thr) insert(s, static_cast<uint32_t>(row0 + j));
+      if (s >= thr) insert(s, static_cast<uint32_t>(row0 + j));  // no-op unless it ranks in
     }
+  }
+
+  static __device__ __forceinline__ bool dry_ok(const TcArgs&) { return true; }
+  // Dry tile: only the published best moves.
+  __device__ __forceinline__ void dry(const uint32_t (&r)[32], int nvalid, bool qvalid) {
+    if (qvalid) best = fmaxf(best, max_valid(r, nvalid));
   }
 
   static __device__ __forceinline__ int jrank(int, int) { return 1; }  // publishes its best
@@ -222,6 +262,7 @@ struct EpiTopkBuf {
   float bound;      // shared lower bound of the query (refreshed per tile)
   float best;       // value this list publishes: a lower bound on its J-th best
   float tj[kRegJ];  // best kRegJ scores appended so far, descending
+  bool redo;        // second pass over dry tiles: their scores are already in tj
   uint32_t published;
   uint32_t top_published;
 
@@ -234,6 +275,7 @@ struct EpiTopkBuf {
     best = -INFINITY;
 #pragma unroll
     for (int i = 0; i < kRegJ; ++i) tj[i] = -INFINITY;
+    redo = false;
     published = 0;
     top_published = 0;
   }
@@ -314,20 +356,31 @@ struct EpiTopkBuf {
   __device__ __forceinline__ void consume(const uint32_t (&r)[32], int row0, int nvalid,
                                           bool qvalid, uint32_t*) {
     const float mx = max32(r);
-    if (qvalid && mx > thr && mx >= bound) {
-      uint32_t m = above_mask(r, thr, bound, nvalid);
+    const float lim = fmaxf(thr, bound);
+    if (qvalid && mx >= lim) {
+      uint32_t m = above_mask(r, lim, nvalid);
       while (m) {
         const int j = __ffs(m) - 1;
         m &= m - 1;
         const float s = pick(r, j);
         list[cnt++] = make_key(s, static_cast<uint32_t>(row0 + j));
-        track(s);
+        if (!redo) track(s);
       }
     }
   }
 
-  // The list holds at least J rows scoring >= best; m = ceil(k / J) lists
-  // reaching a value v therefore prove k rows >= v.
+  // Dry tiles need the J-th best in registers.
+  static __device__ __forceinline__ bool dry_ok(const TcArgs& a) { return tops_j(a.k, a.segs * kSubs) <= kRegJ; }
+  __device__ __forceinline__ void dry(const uint32_t (&r)[32], int nvalid, bool qvalid) {
+    if (!qvalid) return;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nvalid) track(__uint_as_float(r[j]));
+  }
+
+  // The list's segment holds at least J rows scoring >= best (the value is the
+  // J-th best of the rows seen so far); m = ceil(k / J) lists reaching a value v
+  // therefore prove k rows >= v.
   __device__ __forceinline__ void publish_top(const TcArgs& a, int q, int list_idx, int lists) {
     if (jr <= kRegJ) best = fmaxf(best, reg_jth());
     if (best == -INFINITY) return;

@@ -17,6 +17,10 @@ constexpr int kTcN = 256;          // corpus rows per tile (MMA N; TMEM columns)
 constexpr int kTcK = 64;           // halves per K slice (one 128-byte swizzled row)
 constexpr int kTcStages = 4;
 constexpr int kTcMaxResidentSlices = 7;  // queries stay in smem when d_pad <= 448
+// Dry tiles of the top-k epilogues (see cvs_epilogue.cuh): how many, and the
+// tiles a CTA must expect before they pay.
+constexpr int kDryTiles = 2;
+constexpr int kDryMinTiles = 8;
 
 enum TcEpilogue : int {
   kEpiTopkReg16 = 0,   // k <= 16: per-query sorted list in registers
@@ -41,6 +45,9 @@ struct TcArgs {
   uint32_t* gthr;     // [b] shared per-query lower bounds (ordered bits), zeroed per call
   uint32_t* tops;     // [b][segs * lists per segment] each list's published score (ordered bits), zeroed per call
   int* counts;        // [b][segs * lists per segment] keys each buffer list ends with (buffer epilogue)
+  int* tile_counter;  // [qtiles] next unclaimed corpus tile per query tile, zeroed per call;
+                      // null: CTA s works on the fixed tiles [s*tiles_per_seg, (s+1)*tiles_per_seg)
+  int dry;            // tiles each CTA reads dry first (0 or kDryTiles)
   void* scores_out;   // [b][n] fp32/fp16 for the store epilogues
   int* err;           // device error word
 };

@@ -28,6 +28,7 @@
 #include "cvs_device.cuh"
 #include "cvs_epilogue.cuh"
 #include "cvs_kernels.h"
+#include "cvs_sched.cuh"
 #include "cvs_select.cuh"
 
 namespace cvs {
@@ -50,6 +51,7 @@ struct PairLayout {
   int stages;       // offset of the stage ring (after resident queries)
   int stage_bytes;
   int bars;
+  int log;
   int hist;
   int scratch;
   int total;
@@ -61,7 +63,8 @@ __host__ __device__ constexpr PairLayout pair_layout(bool qres, int ksl, int sub
   l.stages = qres ? ksl * kQSlice : 0;
   l.bars = l.stages + pair_stages(scratch_keys) * l.stage_bytes;
   // full[6], empty[6], tfull[2], tempty[2], qfull, done; tmem holder, abort
-  l.hist = l.bars + 8 * (2 * kStages + 6) + 16;
+  l.log = l.bars + 8 * (2 * kStages + 6) + 16;
+  l.hist = l.log + 8 * kLogSlots;
   l.scratch = l.hist + pair_epi_warps(subs) * 256 * 4;
   l.total = l.scratch + pair_epi_warps(subs) * scratch_keys * 8;
   return l;
@@ -86,6 +89,7 @@ struct PairShared {
   __device__ volatile int* abort_flag() const {
     return reinterpret_cast<volatile int*>(base + l.bars + 8 * (2 * kStages + 6) + 4);
   }
+  __device__ uint64_t* log() const { return reinterpret_cast<uint64_t*>(base + l.log); }
   __device__ uint32_t* hist(int w) const { return reinterpret_cast<uint32_t*>(base + l.hist) + 256 * w; }
   __device__ uint64_t* scratch(int w, int keys) const {
     return reinterpret_cast<uint64_t*>(base + l.scratch) + static_cast<size_t>(keys) * w;
@@ -114,7 +118,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
   const int qrow0 = qp * (2 * kTcM) + static_cast<int>(rank) * kTcM;  // this CTA's queries
   const int t_begin = seg * a.tiles_per_seg;
   const int t_end = min(a.ntiles, t_begin + a.tiles_per_seg);
-  const int ntl = max(0, t_end - t_begin);
+  int nd = 0;  // dry tiles (see kDryTiles): the first nd claimed tiles, revisited at the end
+  if constexpr (Epi::kTops) nd = Epi::dry_ok(a) ? a.dry : 0;
   volatile int* abort = sh.abort_flag();
 
   if (threadIdx.x == 0) {
@@ -128,6 +133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
     }
     mbar_init(sh.qfull(), 1);
     mbar_init(sh.done(), 1);
+    log_init(sh.log());
     *abort = 0;
     fence_barrier_init();
   }
@@ -161,10 +167,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
         for (int ks = 0; ks < a.ksl; ++ks) load(sh.qres(ks), &qmap, sh.qfull(), ks * kTcK, qrow0, pol_q);
       }
       const uint32_t tx = QRES ? kXHalf : (kXHalf + kQSlice);
+      // The even CTA claims the pair's tiles and logs them in both CTAs.
+      TileSource src;
+      src.init(a.tile_counter ? a.tile_counter + qp : nullptr, a.ntiles, t_begin, t_end, nd);
+      const uint32_t peer_log = map_to_rank(smem_u32(sh.log()), 1);
       int it = 0;
       bool ok = true;
-      for (int t = 0; t < ntl && ok; ++t) {
-        const int row0 = (t_begin + t) * kTcN + static_cast<int>(rank) * kRows;
+      for (int t = 0; ok; ++t) {
+        uint32_t v;
+        if (leader) {
+          v = src.next();
+          log_put(sh.log(), t, v);
+          log_put_remote(peer_log, t, v);
+        } else if (!log_get(sh.log(), t, &v, abort, a.err, 15)) {
+          ok = false;
+          break;
+        }
+        if (v == kLogEnd) break;
+        const int row0 = static_cast<int>(v & kLogTileMask) * kTcN + static_cast<int>(rank) * kRows;
         for (int ks = 0; ks < a.ksl; ++ks, ++it) {
           const int s = it % kS;
           const uint32_t ph = (it / kS) & 1;
@@ -195,7 +215,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
         bool ok = true;
         if (QRES) ok = mbar_wait(sh.qfull(), 0, abort, a.err, 12);
         int it = 0;
-        for (int t = 0; t < ntl && ok; ++t) {
+        for (int t = 0; ok; ++t) {
+          uint32_t v;
+          if (!log_get(sh.log(), t, &v, abort, a.err, 16)) {
+            ok = false;
+            break;
+          }
+          if (v == kLogEnd) break;
           const int acc = t & 1;
           const uint32_t use = static_cast<uint32_t>(t >> 1);
           if (!mbar_wait(sh.tempty(acc), (use & 1) ^ 1, abort, a.err, 13)) {
@@ -249,21 +275,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
         epi.list = a.part + (static_cast<size_t>(q) * a.segs * Epi::kSubs + seg * Epi::kSubs + sub) * a.cap;
     }
     bool ok = true;
-    for (int t = 0; t < ntl; ++t) {
+    for (int t = 0;; ++t) {
+      uint32_t v = 0;
+      int got = 1;
+      if (lane == 0) got = log_get(sh.log(), t, &v, abort, a.err, 18) ? 1 : 0;
+      got = __shfl_sync(kFullMask, got, 0);
+      v = __shfl_sync(kFullMask, v, 0);
+      if (!got) {
+        ok = false;
+        break;
+      }
+      if (v == kLogEnd) break;
+      const bool dry = (v & kLogDry) != 0;
       const int acc = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
       float fresh = -INFINITY;
       if constexpr (!is_store<Epi>::value) {
-        if (qvalid) fresh = load_bound(a.gthr + q);
+        // Overlaps the wait below, except on the first real tile after dry
+        // tiles: that tile reads the bound after its wait, by which time the
+        // other lists' refresh after the last dry tile has landed.
+        if (qvalid && (t != nd || nd == 0)) fresh = load_bound(a.gthr + q);
       }
       if (!mbar_wait(sh.tfull(acc), use & 1, abort, a.err, 17)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if constexpr (!is_store<Epi>::value) epi.bound = fmaxf(epi.bound, fresh);
-      const int row0 = (t_begin + t) * kTcN;
+      if constexpr (!is_store<Epi>::value) {
+        if (qvalid && t == nd && nd > 0) fresh = load_bound(a.gthr + q);
+        epi.bound = fmaxf(epi.bound, fresh);
+      }
+      const int row0 = static_cast<int>(v & kLogTileMask) * kTcN;
       const int valid = min(kTcN, a.n - row0);
+      if constexpr (std::is_same<Epi, EpiTopkBuf>::value) epi.redo = (v & kLogRedo) != 0;
       for (int c = sub * kChunks; c < (sub + 1) * kChunks; ++c) {
         if (c * 32 >= valid) break;
         uint32_t r[32];
@@ -272,6 +316,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
         const int nv = min(32, valid - c * 32);
         if constexpr (is_store<Epi>::value) {
           epi.consume_store(r, row0 + c * 32, nv, qvalid, a, q);
+        } else if (dry) {
+          epi.dry(r, nv, qvalid);
         } else {
           epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
           if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
@@ -297,7 +343,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
         if (tops_round(t) && lists <= 32 * kTopsPerLane) {
           // This round's refresher of each query raises the query's shared bound
           // to the k-th largest published maximum; the whole warp serves each.
-          unsigned need = __ballot_sync(kFullMask, qvalid && tops_refresher(q, t, list, lists));
+          unsigned need = __ballot_sync(kFullMask, qvalid && tops_refresher(q, t, list, lists, dry ? kDryRefreshers : 1));
           while (need) {
             const int src = __ffs(need) - 1;
             need &= need - 1;

@@ -23,6 +23,7 @@
 #include "cvs_device.cuh"
 #include "cvs_epilogue.cuh"
 #include "cvs_kernels.h"
+#include "cvs_sched.cuh"
 #include "cvs_select.cuh"
 
 namespace cvs {
@@ -50,6 +51,7 @@ struct Layout {
   int stages;     // ring of stages
   int stage_bytes;
   int bars;       // mbarriers
+  int log;        // iteration log (cvs_sched.cuh)
   int hist;       // per epilogue warp radix histograms
   int scratch;    // per epilogue warp compaction buffers (buffer epilogue)
   int total;
@@ -62,7 +64,8 @@ __host__ __device__ constexpr Layout make_layout(bool qres, int ksl, int subs, i
   l.stages = qres ? ksl * kQSliceBytes : 0;
   l.bars = l.stages + num_stages(qres, scratch_keys) * l.stage_bytes;
   // full[4], empty[4], tfull[2], tempty[2], qfull, done, tmem holder, abort
-  l.hist = l.bars + 8 * (2 * kTcStages + 6) + 16;
+  l.log = l.bars + 8 * (2 * kTcStages + 6) + 16;
+  l.hist = l.log + 8 * kLogSlots;
   l.scratch = l.hist + epi_warps(subs) * 256 * 4;
   l.total = l.scratch + epi_warps(subs) * scratch_keys * 8;
   return l;
@@ -89,6 +92,7 @@ struct Shared {
   __device__ volatile int* abort_flag() const {
     return reinterpret_cast<volatile int*>(base + l.bars + 8 * (2 * kTcStages + 6) + 4);
   }
+  __device__ uint64_t* log() const { return reinterpret_cast<uint64_t*>(base + l.log); }
   __device__ uint32_t* hist(int w) const {
     return reinterpret_cast<uint32_t*>(base + l.hist) + 256 * w;
   }
@@ -117,7 +121,8 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
   const int seg = blockIdx.x / a.qtiles;
   const int t_begin = seg * a.tiles_per_seg;
   const int t_end = min(a.ntiles, t_begin + a.tiles_per_seg);
-  const int ntl = max(0, t_end - t_begin);
+  int nd = 0;  // dry tiles (see kDryTiles): the first nd claimed tiles, revisited at the end
+  if constexpr (Epi::kTops) nd = Epi::dry_ok(a) ? a.dry : 0;
   volatile int* abort = sh.abort_flag();
 
   if (threadIdx.x == 0) {
@@ -131,6 +136,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     }
     mbar_init(sh.qfull(), 1);
     mbar_init(sh.done(), 1);
+    log_init(sh.log());
     *abort = 0;
     fence_barrier_init();
   }
@@ -159,10 +165,15 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
           tma_load_2d(sh.qres(ks), &qmap, sh.qfull(), ks * kTcK, qrow0, pol_q);
       }
       const uint32_t tx = QRES ? kXSliceBytes : (kXSliceBytes + kQSliceBytes);
+      TileSource src;
+      src.init(a.tile_counter ? a.tile_counter + qt : nullptr, a.ntiles, t_begin, t_end, nd);
       int it = 0;
       bool ok = true;
-      for (int t = 0; t < ntl && ok; ++t) {
-        const int row0 = (t_begin + t) * kTcN;
+      for (int t = 0; ok; ++t) {
+        const uint32_t v = src.next();
+        log_put(sh.log(), t, v);
+        if (v == kLogEnd) break;
+        const int row0 = static_cast<int>(v & kLogTileMask) * kTcN;
         for (int ks = 0; ks < a.ksl; ++ks, ++it) {
           const int s = it % kS;
           const uint32_t ph = (it / kS) & 1;
@@ -190,7 +201,13 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
       bool ok = true;
       if (QRES) ok = mbar_wait(sh.qfull(), 0, abort, a.err, 2);
       int it = 0;
-      for (int t = 0; t < ntl && ok; ++t) {
+      for (int t = 0; ok; ++t) {
+        uint32_t v;
+        if (!log_get(sh.log(), t, &v, abort, a.err, 6)) {
+          ok = false;
+          break;
+        }
+        if (v == kLogEnd) break;
         const int acc = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
         if (!mbar_wait(sh.tempty(acc), (use & 1) ^ 1, abort, a.err, 3)) {
@@ -240,21 +257,39 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         epi.list = a.part + (static_cast<size_t>(q) * a.segs * Epi::kSubs + seg * Epi::kSubs + sub) * a.cap;
     }
     bool ok = true;
-    for (int t = 0; t < ntl; ++t) {
+    for (int t = 0;; ++t) {
+      uint32_t v = 0;
+      int got = 1;
+      if (lane == 0) got = log_get(sh.log(), t, &v, abort, a.err, 7) ? 1 : 0;
+      got = __shfl_sync(kFullMask, got, 0);
+      v = __shfl_sync(kFullMask, v, 0);
+      if (!got) {
+        ok = false;
+        break;
+      }
+      if (v == kLogEnd) break;
+      const bool dry = (v & kLogDry) != 0;
       const int acc = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
       float fresh = -INFINITY;
       if constexpr (!is_store<Epi>::value) {
-        if (qvalid) fresh = load_bound(a.gthr + q);  // overlaps the wait below
+        // Overlaps the wait below, except on the first real tile after dry
+        // tiles: that tile reads the bound after its wait, by which time the
+        // other lists' refresh after the last dry tile has landed.
+        if (qvalid && (t != nd || nd == 0)) fresh = load_bound(a.gthr + q);
       }
       if (!mbar_wait(sh.tfull(acc), use & 1, abort, a.err, 5)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if constexpr (!is_store<Epi>::value) epi.bound = fmaxf(epi.bound, fresh);
-      const int row0 = (t_begin + t) * kTcN;
+      if constexpr (!is_store<Epi>::value) {
+        if (qvalid && t == nd && nd > 0) fresh = load_bound(a.gthr + q);
+        epi.bound = fmaxf(epi.bound, fresh);
+      }
+      const int row0 = static_cast<int>(v & kLogTileMask) * kTcN;
       const int valid = min(kTcN, a.n - row0);
+      if constexpr (std::is_same<Epi, EpiTopkBuf>::value) epi.redo = (v & kLogRedo) != 0;
       for (int c = sub * kChunks; c < (sub + 1) * kChunks; ++c) {
         if (c * 32 >= valid) break;
         uint32_t r[32];
@@ -263,6 +298,8 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         const int nv = min(32, valid - c * 32);
         if constexpr (is_store<Epi>::value) {
           epi.consume_store(r, row0 + c * 32, nv, qvalid, a, q);
+        } else if (dry) {
+          epi.dry(r, nv, qvalid);
         } else {
           epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
           if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
@@ -285,7 +322,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         if (tops_round(t) && lists <= 32 * kTopsPerLane) {
           // This round's refresher of each query raises the query's shared bound
           // to the k-th largest published maximum; the whole warp serves each.
-          unsigned need = __ballot_sync(kFullMask, qvalid && tops_refresher(q, t, list, lists));
+          unsigned need = __ballot_sync(kFullMask, qvalid && tops_refresher(q, t, list, lists, dry ? kDryRefreshers : 1));
           while (need) {
             const int src = __ffs(need) - 1;
             need &= need - 1;
