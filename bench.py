@@ -18,6 +18,7 @@ bounded sample of the same workload, scaled to the same unit.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -182,7 +183,7 @@ def make_queries(torch, b, d, seed, device):
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -197,30 +198,42 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "20"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:  # nvidia-smi missing: report no clocks
             self.proc = None
 
-    def stop(self):
+    def stop(self, window=None):
+        """Summary of the samples taken inside `window` = (start, end) host times
+        (time.time()) of the timed region; all samples if fewer than 3 fall in it."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.1)
         self.proc.terminate()
         self.proc.wait(timeout=10)
         rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
+            if len(parts) >= 10:
+                try:
+                    parts[0] = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    parts[0] = None
                 rows.append(parts)
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        inside = rows
+        if window is not None:
+            sel = [r for r in rows if r[0] is not None and window[0] <= r[0] <= window[1]]
+            inside = sel if len(sel) >= 3 else rows
+        sm = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in inside if r[3].replace(".", "").isdigit()]
+        pw = [float(r[4]) for r in inside if r[4].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[j] for r in rows for j in range(4) if r[5 + j].lower() == "active"})
+        reasons = sorted({names[j] for r in inside for j in range(4) if r[6 + j].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(inside), "power_w_median": statistics.median(pw) if pw else None,
+                "window": "timed region" if inside is not rows else "whole run (too few samples inside)"}
 
 
 def run_ours(args, cfg):
@@ -279,12 +292,14 @@ def run_ours(args, cfg):
     clocks.start()
     time.sleep(0.3)
     barrier()
+    host_t0 = time.time()
     t0.record(stream)
     for s in range(args.steps):
         mod.set_profile_events(ev_pairs[s][0].cuda_event, ev_pairs[s][1].cuda_event)
         step(q_dev)
     t1.record(stream)
     barrier()
+    host_t1 = time.time()
     mod.set_profile_events(0, 0)
     ms_total = t0.elapsed_time(t1)
     kern_ms = [a.elapsed_time(bb) for a, bb in ev_pairs]
@@ -293,12 +308,17 @@ def run_ours(args, cfg):
     e2e_t0, e2e_t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e2e_t0.record(stream)
+    # Each step's results land in pinned host buffers (stream-ordered copies); the
+    # barrier after the loop waits for the last of them.
+    v_host = torch.empty((b, k), dtype=torch.float32, pin_memory=True)
+    i_host = torch.empty((b, k), dtype=torch.int64, pin_memory=True)
     for _ in range(args.steps):
         v, i = index.search(q_host, k)
-        v_host, i_host = v.cpu(), i.cpu()
+        v_host.copy_(v, non_blocking=True)
+        i_host.copy_(i, non_blocking=True)
     e2e_t1.record(stream)
     barrier()
-    clk = clocks.stop()
+    clk = clocks.stop(window=(host_t0, host_t1))
     e2e_ms_total = e2e_t0.elapsed_time(e2e_t1)
 
     tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)], dtype=torch.float64, device=dev)

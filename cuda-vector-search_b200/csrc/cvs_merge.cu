@@ -23,7 +23,7 @@ constexpr int kMergeWarps = 2;       // queries per CTA of the list merge
 constexpr int kMergeMaxK = 1024;
 constexpr int kKeysThreads = 256;     // one CTA (8 warps) per query in the key merge
 constexpr int kKeysWarps = kKeysThreads / 32;
-constexpr int kKeysBatch = 16;        // 32-key rows in flight per warp
+constexpr int kKeysBatch = 8;         // keys in flight per lane
 constexpr int kMergeTopsPerLane = 16;  // up to 512 lists per query
 
 // Shared memory per warp of the list merge: radix histogram, k selected keys.
@@ -33,9 +33,12 @@ __host__ __device__ constexpr size_t merge_warp_bytes(int k) {
 
 // Survivors of the bound filter kept in shared memory (4k, at least 512).
 __host__ __device__ constexpr int survivor_cap(int k) { return 4 * k > 512 ? 4 * k : 512; }
-// Key-merge CTA: histogram, k selected keys, survivors, two counters and the bound.
+constexpr int kScanLists = 1024;      // counted lists merged through the offset scan
+// Key-merge CTA: histogram, k selected keys, survivors, two counters and the
+// bound, per-warp scan totals, list offsets.
 __host__ __device__ constexpr size_t keys_smem(int k) {
-  return 256 * 4 + static_cast<size_t>(k) * 8 + static_cast<size_t>(survivor_cap(k)) * 8 + 16;
+  return 256 * 4 + static_cast<size_t>(k) * 8 + static_cast<size_t>(survivor_cap(k)) * 8 + 16 +
+         kKeysWarps * 4 + kScanLists * 4;
 }
 
 // Keys of one query: `lists` lists of `stride` slots, of which the first
@@ -113,8 +116,8 @@ __device__ void select_and_emit(const Acc& acc, int m, int k, long long id_offse
 
 // One CTA per query. Warp 0 forms the query's bound: the kernel's running
 // bound (a.bounds) raised to the tops_m-th largest per-list published score.
-// All eight warps then stream the query's lists in 32-key rows (16 rows in
-// flight per warp) and append the keys at or above the bound -- typically one
+// All eight warps then walk the query's lists, one list per lane up to its key
+// count (eight loads in flight), and append the keys at or above the bound -- typically one
 // to three times k of them -- to a shared survivor buffer; warp 0 radix-selects
 // the k-th best survivor, the k winners are gathered, and every thread writes
 // some of them straight to their output rank (the number of larger winners).
@@ -131,6 +134,11 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
   uint64_t* surv = sel + a.k;
   int* s_cnt = reinterpret_cast<int*>(surv + scap);  // [0] survivors, [1] winners
   uint32_t* s_bound = reinterpret_cast<uint32_t*>(s_cnt + 2);
+  int* s_warp = reinterpret_cast<int*>(s_bound + 2);  // [kKeysWarps]
+  int* s_off = s_warp + kKeysWarps;                   // [kScanLists]
+  // Launched as a programmatic dependent of the search kernel: everything the
+  // search kernel wrote is visible once this returns.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint64_t* base = a.part + static_cast<size_t>(q) * a.lists * a.stride;
   const int* counts = a.counts ? a.counts + static_cast<size_t>(q) * a.lists : nullptr;
   float* out_v = a.out_v + static_cast<size_t>(q) * a.k;
@@ -159,25 +167,9 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
     return;
   }
 
-  // Rows of 32 slots: counted lists are walked list by list (row r of list l
-  // covers slots 32r..32r+31), uniform lists as one contiguous run.
-  const int L = counts ? a.lists : 1;
-  const int S = counts ? a.stride : a.lists * a.per_list;
-  const int R = (S + 31) / 32;
-  const int rows = L * R;
-  for (int r0 = warp * kKeysBatch; r0 < rows; r0 += kKeysWarps * kKeysBatch) {
-    uint64_t keys[kKeysBatch];
-#pragma unroll
-    for (int u = 0; u < kKeysBatch; ++u) {
-      const int row = r0 + u;
-      keys[u] = 0ull;
-      if (row < rows) {
-        const int l = row / R;
-        const int j = (row - l * R) * 32 + lane;
-        const int used = counts ? min(counts[l], S) : S;
-        if (j < used) keys[u] = base[static_cast<size_t>(l) * S + j];
-      }
-    }
+  const int S = a.stride;
+  // Appends the keys of one batch that are at or above the bound (whole warp).
+  auto keep_batch = [&](const uint64_t (&keys)[kKeysBatch]) {
 #pragma unroll
     for (int u = 0; u < kKeysBatch; ++u) {
       const bool keep = keys[u] != 0ull && static_cast<uint32_t>(keys[u] >> 32) >= bound;
@@ -187,6 +179,86 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
         if (lane == __ffs(bal) - 1) pos = atomicAdd(s_cnt, __popc(bal));
         pos = __shfl_sync(kFullMask, pos, __ffs(bal) - 1) + __popc(bal & ((1u << lane) - 1u));
         if (keep && pos < scap) surv[pos] = keys[u];
+      }
+    }
+  };
+  if (counts == nullptr || a.lists <= kScanLists) {
+    // The used keys as one flat run: packed lists directly, counted lists
+    // through a block-wide exclusive scan of their counts (s_off) and a binary
+    // search per key. Every thread keeps eight loads in flight.
+    int total;
+    if (counts == nullptr) {
+      total = a.lists * a.per_list;
+    } else {
+      const int per = (a.lists + kKeysThreads - 1) / kKeysThreads;  // <= kScanLists / 256
+      int mine[kScanLists / kKeysThreads];
+      int sum = 0;
+#pragma unroll
+      for (int u = 0; u < kScanLists / kKeysThreads; ++u) {
+        const int l = threadIdx.x * per + u;
+        mine[u] = (u < per && l < a.lists) ? min(max(counts[l], 0), S) : 0;
+        sum += mine[u];
+      }
+      int incl = sum;  // warp inclusive scan, then across warps
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (lane == 31) s_warp[warp] = incl;
+      __syncthreads();
+      int before = 0;
+      total = 0;
+#pragma unroll
+      for (int w = 0; w < kKeysWarps; ++w) {
+        const int t = s_warp[w];
+        before += w < warp ? t : 0;
+        total += t;
+      }
+      int excl = before + incl - sum;
+#pragma unroll
+      for (int u = 0; u < kScanLists / kKeysThreads; ++u) {
+        const int l = threadIdx.x * per + u;
+        if (u < per && l < a.lists) s_off[l] = excl;
+        excl += mine[u];
+      }
+      __syncthreads();
+    }
+    for (int i0 = 0; i0 < total; i0 += kKeysThreads * kKeysBatch) {
+      uint64_t keys[kKeysBatch];
+#pragma unroll
+      for (int u = 0; u < kKeysBatch; ++u) {
+        const int i = i0 + u * kKeysThreads + static_cast<int>(threadIdx.x);
+        keys[u] = 0ull;
+        if (i < total) {
+          if (counts == nullptr) {
+            keys[u] = base[i];
+          } else {
+            int lo = 0, hi = a.lists - 1;  // last list whose offset is <= i
+            while (lo < hi) {
+              const int mid = (lo + hi + 1) >> 1;
+              if (s_off[mid] <= i) lo = mid;
+              else hi = mid - 1;
+            }
+            keys[u] = base[static_cast<size_t>(lo) * S + (i - s_off[lo])];
+          }
+        }
+      }
+      keep_batch(keys);
+    }
+  } else {
+    // Many counted lists: lane l of warp w walks list 32 * (8g + w) + l up to
+    // its count, eight keys in flight per lane.
+    for (int l0 = warp * 32; l0 < a.lists; l0 += kKeysWarps * 32) {
+      const int l = l0 + lane;
+      const int used = l < a.lists ? min(max(counts[l], 0), S) : 0;
+      const int most = __reduce_max_sync(kFullMask, used);
+      const uint64_t* lp = base + static_cast<size_t>(l) * S;
+      for (int j0 = 0; j0 < most; j0 += kKeysBatch) {
+        uint64_t keys[kKeysBatch];
+#pragma unroll
+        for (int u = 0; u < kKeysBatch; ++u) keys[u] = (j0 + u < used) ? lp[j0 + u] : 0ull;
+        keep_batch(keys);
       }
     }
   }
@@ -257,8 +329,19 @@ cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  merge_keys_kernel<<<static_cast<unsigned>(a.b), kKeysThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the merge grid may be scheduled while the
+  // search kernel's last CTAs finish (it waits for their results on the device).
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.b), 1, 1);
+  cfg.blockDim = dim3(kKeysThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_keys_kernel, a);
 }
 
 cudaError_t merge_lists_launch(const MergeListsArgs& a, cudaStream_t stream) {
