@@ -71,6 +71,7 @@ cudaError_t tc_pair_launch(int epi, bool resident_queries, const CUtensorMap* qm
 // ---- CUDA-core GEMV + top-k for batches of at most 8 queries ---------------
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxK = 32;
+constexpr int kGemvAutoMaxBatch = 2;  // automatic plans use the GEMV up to this batch
 
 struct GemvArgs {
   const __half* x;    // [n][d_pad]

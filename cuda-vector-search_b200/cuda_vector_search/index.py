@@ -144,7 +144,7 @@ class Index:
         """Return (scores [b, k] float32, ids [b, k] int64), best first.
 
         method:
-            "fused"   - tcgen05 (or GEMV for b <= 8) scores + top-k in one pass (k <= 1024)
+            "fused"   - tcgen05 (or GEMV for b <= 2) scores + top-k in one pass (k <= 1024)
             "twopass" - score kernel writes the full matrix, then torch.topk
             "torch"   - torch.matmul (cuBLAS) + torch.topk
             "auto"    - fused when k <= 1024, else twopass
