@@ -189,9 +189,9 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
   if (k > n) return fail(CVS_ERR_INVALID_ARGUMENT, "k (%d) must not exceed the corpus size (%lld)", k, (long long)n);
   if (chunks < 0) return fail(CVS_ERR_INVALID_ARGUMENT, "chunks must be >= 0");
   // bq = 0 (automatic): the CUDA-core GEMV for batches of at most
-  // kGemvAutoMaxBatch queries (beyond that the tcgen05 kernel streams the corpus
+  // kGemvMaxBatch queries (beyond that the tcgen05 kernel streams the corpus
   // faster); an explicit bq asks for the tcgen05 tiles whatever the batch.
-  if (bq == 0 && b <= kGemvAutoMaxBatch && gemv_supported(static_cast<int>(b), k, d_pad)) {
+  if (bq == 0 && gemv_supported(static_cast<int>(b), k, d_pad)) {
     p->gemv = true;
     int segs = chunks > 0 ? chunks : dev.sms * gemv_blocks_per_sm(static_cast<int>(b), d_pad);
     segs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(segs, n)));

@@ -1,6 +1,7 @@
-// CUDA-core GEMV + top-k for small batches (b <= 8, k <= 32): the HBM-bound
-// case. Replaces the reference's fused kernel at bq=16 for tiny batches
-// (cuda_vector_search/csrc/kernels.cu:313-371 run with nq <= 8, where 15 of
+// CUDA-core GEMV + top-k for one or two queries (k <= 32): the HBM-bound case.
+// From three queries on, the per-row arithmetic of this kernel exceeds the
+// corpus stream and the tcgen05 kernel is faster. Replaces the reference's fused kernel at bq=16 for tiny batches
+// (cuda_vector_search/csrc/kernels.cu:313-371 run with nq <= 2, where 14 of
 // its 16 query rows are padding).
 //
 // Each warp owns whole corpus rows: lane l reads 16-byte chunks l, l+32, ... of
@@ -183,8 +184,7 @@ using GemvKernel = void (*)(const GemvArgs);
 
 template <int NQ, int CPL>
 GemvKernel kernel_cpl() {
-  constexpr int R = NQ <= 2 ? 4 : 2;
-  return gemv_topk_kernel<NQ, CPL, R>;
+  return gemv_topk_kernel<NQ, CPL, 4>;
 }
 
 template <int NQ>
@@ -198,19 +198,14 @@ GemvKernel kernel_nq(int d_pad) {
   }
 }
 
-// The instantiation for b queries of width d_pad: NQ = b rounded up to 1/2/4/8,
-// CPL = 16-byte chunks per lane per row.
-GemvKernel select_kernel(int b, int d_pad) {
-  if (b == 1) return kernel_nq<1>(d_pad);
-  if (b == 2) return kernel_nq<2>(d_pad);
-  if (b <= 4) return kernel_nq<4>(d_pad);
-  return kernel_nq<8>(d_pad);
-}
+// The instantiation for b (1 or 2) queries of width d_pad; CPL = 16-byte chunks
+// per lane per row.
+GemvKernel select_kernel(int b, int d_pad) { return b == 1 ? kernel_nq<1>(d_pad) : kernel_nq<2>(d_pad); }
 
 }  // namespace
 
 bool gemv_supported(int b, int k, int d_pad) {
-  return b >= 1 && b <= 8 && k >= 1 && k <= kGemvMaxK && d_pad >= 64 && d_pad <= 1024;
+  return b >= 1 && b <= kGemvMaxBatch && k >= 1 && k <= kGemvMaxK && d_pad >= 64 && d_pad <= 1024;
 }
 
 // Resident blocks per SM of the instantiation that gemv_launch will use, so the
