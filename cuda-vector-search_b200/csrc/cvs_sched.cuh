@@ -78,6 +78,9 @@ __device__ __forceinline__ bool log_get(const uint64_t* log, int iter, uint32_t*
       report_error(err, kErrTimeout | site);
       return false;
     }
+    // Back off so a waiting reader does not take issue slots from the producer
+    // and MMA warps sharing its scheduler.
+    __nanosleep(64);
   }
 }
 
