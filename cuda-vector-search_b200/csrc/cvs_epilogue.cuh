@@ -112,10 +112,9 @@ constexpr int kTopsPerLane = 10;  // lists per query <= 320 for the in-kernel re
 // Instead the first kDryTiles tiles a CTA works on are read "dry" -- they only
 // raise the value each list publishes for the query's bound -- and are computed
 // again, for real, after the CTA's last tile, when the bound from every list's
-// first tiles is in place. The host sets the count (TcArgs::dry): kDryTiles
-// when a CTA can expect at least kDryMinTiles tiles (the extra MMA work is
-// kDryTiles / tiles), one when it expects 2..kDryMinTiles-1; kDryTiles and
-// kDryMinTiles are in cvs_kernels.h.
+// first tiles is in place. The host sets the count (TcArgs::dry, at most
+// kDryTiles from cvs_kernels.h): two when a CTA can expect three or more tiles,
+// one for two; the extra MMA work is the dry count / tiles per CTA.
 
 // Largest of the first nvalid scores.
 __device__ __forceinline__ float max_valid(const uint32_t (&r)[32], int nvalid) {

@@ -17,10 +17,8 @@ constexpr int kTcN = 256;          // corpus rows per tile (MMA N; TMEM columns)
 constexpr int kTcK = 64;           // halves per K slice (one 128-byte swizzled row)
 constexpr int kTcStages = 4;
 constexpr int kTcMaxResidentSlices = 7;  // queries stay in smem when d_pad <= 448
-// Dry tiles of the top-k epilogues (see cvs_epilogue.cuh): how many, and the
-// tiles a CTA must expect before they pay.
+// Dry tiles of the top-k epilogues (see cvs_epilogue.cuh): at most this many.
 constexpr int kDryTiles = 2;
-constexpr int kDryMinTiles = 8;
 
 enum TcEpilogue : int {
   kEpiTopkReg16 = 0,   // k <= 16: per-query sorted list in registers
