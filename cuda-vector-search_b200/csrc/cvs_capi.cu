@@ -307,7 +307,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   const bool prof = g_prof_start && g_prof_stop;
   cudaError_t e;
   // The shared per-query bounds must start at "none" (0) on every call.
-  if (p.clear_bytes && (e = cudaMemsetAsync(bounds, 0, p.clear_bytes, s)) != cudaSuccess)
+  if (p.clear_bytes && (e = clear_launch(bounds, round_up(p.clear_bytes, 4), s)) != cudaSuccess)
     return cuda_fail(e, "clearing the per-query bounds");
   if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   if (p.gemv) {

@@ -92,6 +92,19 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch
+// ---------------------------------------------------------------------------
+// Blocks until the grids this one depends on (the previous kernel on the
+// stream, when launched with programmatic stream serialisation) have completed
+// and their memory is visible; a no-op for an ordinary launch.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel on the stream (if launched programmatically) start its
+// prologue; it still waits for this grid's results with grid_dependency_wait.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // TMA (tiled tensor copies global -> shared, completion on an mbarrier)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {

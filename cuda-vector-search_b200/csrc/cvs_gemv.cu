@@ -69,6 +69,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_topk_kernel(const GemvArgs 
   __shared__ uint64_t cand[NQ][kWarps][kGemvMaxK];
   __shared__ uint32_t hist[kWarps][256];
 
+  // Launched programmatically after the workspace clear: wait for it (and for
+  // the kernels before it) before reading anything.
+  grid_dependency_wait();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int chunks = a.d_pad >> 3;  // 16-byte chunks per row
@@ -232,8 +235,7 @@ cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t stream) {
   if (!gemv_supported(a.b, a.k, a.d_pad)) return cudaErrorInvalidValue;
   GemvKernel k = select_kernel(a.b, a.d_pad);
   if (!k) return cudaErrorInvalidValue;
-  k<<<a.segs, kGemvThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_programmatic(k, dim3(a.segs), dim3(kGemvThreads), 0, stream, a);
 }
 
 }  // namespace cvs

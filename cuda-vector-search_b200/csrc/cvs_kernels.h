@@ -110,6 +110,29 @@ struct MergeKeysArgs {
 };
 cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream);
 
+// Zeroes `bytes` bytes at p (4-byte aligned) and lets the next kernel, launched
+// programmatically, start its prologue meanwhile.
+cudaError_t clear_launch(void* p, size_t bytes, cudaStream_t stream);
+
+// Launches `kernel` with programmatic stream serialisation: it may start while
+// the previous kernel on the stream finishes and must call
+// grid_dependency_wait() before touching that kernel's results.
+template <class... Params, class... Args>
+cudaError_t launch_programmatic(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 struct MergeListsArgs {
   const float* v;        // [lists][b][len] scores
   const long long* ids;  // [lists][b][len] ids (must lie in [0, 2^31))

@@ -11,6 +11,8 @@
 //
 // merge_lists_kernel is the same merge over [lists][b][len] (score, int64 id)
 // arrays, used after the multi-GPU gather of per-shard results.
+#include <algorithm>
+
 #include "cvs_device.cuh"
 #include "cvs_kernels.h"
 #include "cvs_select.cuh"
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
   int* s_off = s_warp + kKeysWarps;                   // [kScanLists]
   // Launched as a programmatic dependent of the search kernel: everything the
   // search kernel wrote is visible once this returns.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  grid_dependency_wait();
   const uint64_t* base = a.part + static_cast<size_t>(q) * a.lists * a.stride;
   const int* counts = a.counts ? a.counts + static_cast<size_t>(q) * a.lists : nullptr;
   float* out_v = a.out_v + static_cast<size_t>(q) * a.k;
@@ -319,6 +321,12 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const Mer
 
 size_t merge_smem(int k) { return kMergeWarps * merge_warp_bytes(k); }
 
+__global__ void __launch_bounds__(256) clear_kernel(uint32_t* p, size_t words) {
+  grid_launch_dependents();
+  for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < words; i += static_cast<size_t>(gridDim.x) * 256)
+    p[i] = 0u;
+}
+
 }  // namespace
 
 cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream) {
@@ -331,17 +339,16 @@ cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   // Programmatic dependent launch: the merge grid may be scheduled while the
   // search kernel's last CTAs finish (it waits for their results on the device).
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(a.b), 1, 1);
-  cfg.blockDim = dim3(kKeysThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, merge_keys_kernel, a);
+  return launch_programmatic(merge_keys_kernel, dim3(static_cast<unsigned>(a.b)), dim3(kKeysThreads), smem,
+                             stream, a);
+}
+
+cudaError_t clear_launch(void* p, size_t bytes, cudaStream_t stream) {
+  const size_t words = bytes / 4;
+  if (words == 0) return cudaSuccess;
+  const unsigned grid = static_cast<unsigned>(std::min<size_t>((words + 255) / 256, 1024));
+  clear_kernel<<<grid, 256, 0, stream>>>(static_cast<uint32_t*>(p), words);
+  return cudaGetLastError();
 }
 
 cudaError_t merge_lists_launch(const MergeListsArgs& a, cudaStream_t stream) {

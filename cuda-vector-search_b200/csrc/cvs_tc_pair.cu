@@ -150,6 +150,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
   cluster_sync_all();  // the partner's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *sh.tmem_holder();
+  // Launched programmatically after the workspace clear (or the caller's previous
+  // kernel): the set-up above overlapped it; everything below reads its results.
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------ TMA producer (both CTAs) ----------------
@@ -388,8 +391,7 @@ cudaError_t pair_launch_one(const CUtensorMap* qmap, const CUtensorMap* xmap, co
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const unsigned grid = 2u * static_cast<unsigned>(a.qtiles) * static_cast<unsigned>(a.segs);
-  kern<<<grid, pair_threads(Epi::kSubs), smem, stream>>>(*qmap, *xmap, a);
-  return cudaGetLastError();
+  return launch_programmatic(kern, dim3(grid), dim3(pair_threads(Epi::kSubs)), smem, stream, *qmap, *xmap, a);
 }
 
 template <bool QRES, class Epi>

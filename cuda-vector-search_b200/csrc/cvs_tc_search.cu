@@ -152,6 +152,9 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *sh.tmem_holder();
+  // Launched programmatically after the workspace clear (or the caller's previous
+  // kernel): the set-up above overlapped it; everything below reads its results.
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -361,8 +364,7 @@ cudaError_t launch_one(const CUtensorMap* qmap, const CUtensorMap* xmap, const T
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const unsigned grid = static_cast<unsigned>(a.qtiles) * static_cast<unsigned>(a.segs);
-  kern<<<grid, tc_threads(Epi::kSubs), smem, stream>>>(*qmap, *xmap, a);
-  return cudaGetLastError();
+  return launch_programmatic(kern, dim3(grid), dim3(tc_threads(Epi::kSubs)), smem, stream, *qmap, *xmap, a);
 }
 
 template <bool QRES>
