@@ -136,3 +136,27 @@ def test_no_device_errors_after_edges(cvs):
 
     torch.cuda.synchronize()
     assert _ext.load().poll_device_error(torch.cuda.current_device()) == 0
+
+
+# Dry tiles (each CTA reads its first one or two claimed tiles twice: once to
+# publish bounds, once for real after its last tile) only appear when a CTA gets
+# at least two tiles; chunk overrides and a larger corpus force every regime:
+# 1 tile per CTA (none), 2 (one dry tile), 3 and more (two).
+@pytest.mark.parametrize("chunks", [0, 3, 8, 30, 60])
+@pytest.mark.parametrize("b,k", [(1, 10), (3, 10), (70, 10), (70, 24), (70, 64), (300, 10), (300, 200)])
+def test_dry_tile_regimes(cvs, chunks, b, k):
+    x, q = _data(120000 if chunks == 0 else 15360, 128, b, seed=chunks * 31 + b + k)
+    _check(cvs, x, q, k, chunks=chunks if chunks else None)
+
+
+@pytest.mark.parametrize("b,expect_gemv", [(1, True), (2, True), (3, False), (8, False)])
+def test_plan_selects_gemv_only_for_one_or_two_queries(cvs, b, expect_gemv):
+    from cuda_vector_search import _ext
+
+    x, q = _data(5000, 256, b, seed=b)
+    index = cvs.Index(x.cuda(), metric="ip")
+    v, i, plan = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, 10)
+    assert (plan.tolist()[0] == b) == expect_gemv  # GEMV plans echo b, tcgen05 plans the tile
+    v2, i2, plan2 = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, 10, 64)
+    assert plan2.tolist()[0] == 64  # an explicit bq always selects tcgen05 tiles
+    assert torch.equal(i, i2)
