@@ -421,11 +421,15 @@ cvs_status cvs_scores(const void* q_f16, int64_t b, const void* x_f16, int64_t n
   return CVS_OK;
 }
 
-cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t lists, int64_t b,
-                           int64_t len, int k, float* out_scores, int64_t* out_ids, void* stream) {
+cvs_status cvs_merge_lists_strided(const float* scores, int64_t scores_list_stride, const int64_t* ids,
+                                   int64_t ids_list_stride, int64_t lists, int64_t b, int64_t len, int k,
+                                   float* out_scores, int64_t* out_ids, void* stream) {
   if (lists < 1 || b < 0 || len < 1 || lists * len >= INT_MAX)
     return fail(CVS_ERR_INVALID_ARGUMENT, "bad list shape [%lld][%lld][%lld]", (long long)lists,
                 (long long)b, (long long)len);
+  if (scores_list_stride < b * len || ids_list_stride < b * len)
+    return fail(CVS_ERR_INVALID_ARGUMENT, "list strides (%lld, %lld) below b * len (%lld)",
+                (long long)scores_list_stride, (long long)ids_list_stride, (long long)(b * len));
   if (k < 1 || k > CVS_MAX_FUSED_K) return fail(CVS_ERR_INVALID_ARGUMENT, "k out of range (%d)", k);
   if (b == 0) return CVS_OK;
   if (!scores || !ids || !out_scores || !out_ids) return fail(CVS_ERR_INVALID_ARGUMENT, "null pointer");
@@ -435,6 +439,8 @@ cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t list
   MergeListsArgs a{};
   a.v = scores;
   a.ids = reinterpret_cast<const long long*>(ids);
+  a.v_stride = scores_list_stride;
+  a.i_stride = ids_list_stride;
   a.b = static_cast<int>(b);
   a.lists = static_cast<int>(lists);
   a.len = static_cast<int>(len);
@@ -445,6 +451,11 @@ cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t list
   cudaError_t e = merge_lists_launch(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
   return CVS_OK;
+}
+
+cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t lists, int64_t b,
+                           int64_t len, int k, float* out_scores, int64_t* out_ids, void* stream) {
+  return cvs_merge_lists_strided(scores, b * len, ids, b * len, lists, b, len, k, out_scores, out_ids, stream);
 }
 
 cvs_status cvs_poll_device_error(int device, int* code) {

@@ -134,8 +134,10 @@ cudaError_t launch_programmatic(void (*kernel)(Params...), dim3 grid, dim3 block
 }
 
 struct MergeListsArgs {
-  const float* v;        // [lists][b][len] scores
-  const long long* ids;  // [lists][b][len] ids (must lie in [0, 2^31))
+  const float* v;        // [lists] x [b][len] scores, lists v_stride floats apart
+  const long long* ids;  // [lists] x [b][len] ids (must lie in [0, 2^31)), lists i_stride apart
+  long long v_stride;
+  long long i_stride;
   int b;
   int lists;
   int len;

@@ -61,14 +61,16 @@ struct PartKeys {
 struct ListKeys {
   const float* v;
   const long long* ids;
-  int b;
+  long long v_stride;
+  long long i_stride;
   int len;
   int q;
   __device__ __forceinline__ uint64_t operator()(int i) const {
-    const size_t o = (static_cast<size_t>(i / len) * b + q) * len + (i % len);
-    const long long id = ids[o];
+    const long long l = i / len;
+    const long long o = static_cast<long long>(q) * len + (i % len);
+    const long long id = ids[l * i_stride + o];
     if (id < 0) return 0ull;  // empty slot
-    return make_key(v[o], static_cast<uint32_t>(id));
+    return make_key(v[l * v_stride + o], static_cast<uint32_t>(id));
   }
 };
 
@@ -314,7 +316,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const Mer
   uint32_t* hist = reinterpret_cast<uint32_t*>(mine);
   uint64_t* sel = reinterpret_cast<uint64_t*>(mine + 256 * 4);
   if (q >= a.b) return;
-  const ListKeys acc{a.v, a.ids, a.b, a.len, q};
+  const ListKeys acc{a.v, a.ids, a.v_stride, a.i_stride, a.len, q};
   select_and_emit(acc, a.lists * a.len, a.k, 0, hist, sel, a.out_v + static_cast<size_t>(q) * a.k,
                   a.out_i + static_cast<size_t>(q) * a.k, lane);
 }

@@ -152,14 +152,18 @@ std::vector<torch::Tensor> merge_lists(torch::Tensor v, torch::Tensor i, int64_t
   TORCH_CHECK(v.dim() == 3 && i.sizes() == v.sizes(), "expects [lists, b, len] scores and ids");
   TORCH_CHECK(v.scalar_type() == torch::kFloat && i.scalar_type() == torch::kLong,
               "scores must be float32 and ids int64");
-  TORCH_CHECK(v.is_contiguous() && i.is_contiguous(), "inputs must be contiguous");
+  // Each [b, len] list must be dense; the lists themselves may be any stride
+  // apart (e.g. views into one gathered buffer per rank).
+  TORCH_CHECK(v.stride(2) == 1 && v.stride(1) == v.size(2) && i.stride(2) == 1 && i.stride(1) == i.size(2),
+              "each [b, len] list must be contiguous");
   const c10::cuda::CUDAGuard guard(v.device());
   const int64_t b = v.size(1);
   auto out_v = torch::empty({b, k}, v.options());
   auto out_i = torch::empty({b, k}, i.options());
-  check(cvs_merge_lists(v.data_ptr<float>(), i.data_ptr<int64_t>(), v.size(0), b, v.size(2),
-                        static_cast<int>(k), out_v.data_ptr<float>(), out_i.data_ptr<int64_t>(),
-                        stream_of(v)),
+  check(cvs_merge_lists_strided(v.data_ptr<float>(), v.size(0) > 1 ? v.stride(0) : b * v.size(2),
+                                i.data_ptr<int64_t>(), i.size(0) > 1 ? i.stride(0) : b * i.size(2), v.size(0),
+                                b, v.size(2), static_cast<int>(k), out_v.data_ptr<float>(),
+                                out_i.data_ptr<int64_t>(), stream_of(v)),
         "merge_lists");
   return {out_v, out_i};
 }

@@ -6,8 +6,10 @@ chunk start, concatenate, top-k again) is the template. Here each rank owns a
 contiguous row range of the corpus, runs the fused search on it with its global
 row offset folded into the ids, the ranks all-gather their [b, k] (score, id)
 lists (NCCL over NVLink), and every rank merges the [world, b, k] lists with the
-merge kernel. There is exactly one collective per search and it carries
-12 * b * k bytes per rank.
+merge kernel. There is exactly one collective per search: each rank's ids and
+scores sit in one block (12 * b * k bytes, rounded up to 8), the search writes
+them there directly, and the merge reads them straight out of the gathered
+blocks.
 
 Ordering is exact and global: score descending, then smaller global id, the same
 rule as the single-GPU index, because every per-rank list is complete for its
@@ -43,37 +45,65 @@ class ShardOps:
 
     local_topk(queries, k, id_offset) -> (scores [b, k] f32, ids [b, k] i64, sorted
     best first, ids already global, empty slots id -1); merge(scores [W, b, k],
-    ids [W, b, k], k) -> (scores [b, k], ids [b, k]).
+    ids [W, b, k], k) -> (scores [b, k], ids [b, k]) (each [b, k] list dense, the W
+    lists any stride apart). local_topk_into(queries, k, id_offset, scores_out,
+    ids_out), if given, writes the local result into the given [b, k] tensors.
     """
 
     local_topk: Callable
     merge: Callable
     n_local: int
     device: torch.device
+    local_topk_into: Callable | None = None
+
+
+def _block_bytes(b: int, k: int) -> int:
+    """One rank's gathered block: b*k int64 ids, then b*k float32 scores, 8-aligned."""
+    return (12 * b * k + 7) // 8 * 8
+
+
+def _block_views(block: torch.Tensor, b: int, k: int):
+    """(scores, ids) views of [..., block_bytes] uint8 block(s) as [..., b, k]."""
+    n = b * k
+    lead = tuple(block.shape[:-1])
+    ids = block[..., : 8 * n].view(torch.int64).view(lead + (b, k))
+    scores = block[..., 8 * n : 12 * n].view(torch.float32).view(lead + (b, k))
+    return scores, ids
 
 
 def cuda_shard_ops(index: Index) -> ShardOps:
     """Operations backed by this package's kernels for one rank's Index."""
     mod = _ext.load()
 
-    def local_topk(queries, k, id_offset):
+    def local_topk_into(queries, k, id_offset, v, i):
         q = index._prep_queries(queries)
         b = q.shape[0]
         kk = min(k, len(index))
-        v = torch.empty((b, kk), dtype=torch.float32, device=index.device)
-        i = torch.empty((b, kk), dtype=torch.int64, device=index.device)
         ws = torch.empty(max(256, mod.workspace_size(b, len(index), index._x.shape[1], kk)),
                          dtype=torch.uint8, device=index.device)
-        mod.fused_topk_into(q, index._x, kk, id_offset, v, i, ws)
-        if kk < k:  # shard smaller than k: pad with empty slots
-            v = torch.cat([v, v.new_full((b, k - kk), float("-inf"))], 1)
-            i = torch.cat([i, i.new_full((b, k - kk), -1)], 1)
+        if kk == k:
+            mod.fused_topk_into(q, index._x, kk, id_offset, v, i, ws)
+        else:  # shard smaller than k: its kk results, then empty slots
+            vk = torch.empty((b, kk), dtype=torch.float32, device=index.device)
+            ik = torch.empty((b, kk), dtype=torch.int64, device=index.device)
+            mod.fused_topk_into(q, index._x, kk, id_offset, vk, ik, ws)
+            v[:, :kk] = vk
+            i[:, :kk] = ik
+            v[:, kk:] = float("-inf")
+            i[:, kk:] = -1
+
+    def local_topk(queries, k, id_offset):
+        b = index._prep_queries(queries).shape[0]
+        v = torch.empty((b, k), dtype=torch.float32, device=index.device)
+        i = torch.empty((b, k), dtype=torch.int64, device=index.device)
+        local_topk_into(queries, k, id_offset, v, i)
         return v, i
 
     def merge(v_all, i_all, k):
-        return mod.merge_lists(v_all.contiguous(), i_all.contiguous(), k)
+        return mod.merge_lists(v_all, i_all, k)
 
-    return ShardOps(local_topk=local_topk, merge=merge, n_local=len(index), device=index.device)
+    return ShardOps(local_topk=local_topk, merge=merge, n_local=len(index), device=index.device,
+                    local_topk_into=local_topk_into)
 
 
 class ShardedIndex:
@@ -119,7 +149,18 @@ class ShardedIndex:
         k = min(k, self.n_total)
         if k > MAX_FUSED_K:
             raise ValueError(f"sharded search supports k <= {MAX_FUSED_K}")
-        v, i = self.ops.local_topk(queries, k, self.row_offset)
-        v_all = all_gather_stacked(v, self.group)
-        i_all = all_gather_stacked(i, self.group)
+        if self.ops.local_topk_into is not None:
+            b = queries.shape[0] if getattr(queries, "ndim", 1) == 2 else 1
+            block = torch.empty(_block_bytes(b, k), dtype=torch.uint8, device=self.ops.device)
+            v, i = _block_views(block, b, k)
+            self.ops.local_topk_into(queries, k, self.row_offset, v, i)
+        else:
+            v, i = self.ops.local_topk(queries, k, self.row_offset)
+            b = v.shape[0]
+            block = torch.empty(_block_bytes(b, k), dtype=torch.uint8, device=v.device)
+            bv, bi = _block_views(block, b, k)
+            bv.copy_(v)
+            bi.copy_(i)
+        gathered = all_gather_stacked(block, self.group)  # [W, block bytes], one collective
+        v_all, i_all = _block_views(gathered, b, k)
         return self.ops.merge(v_all, i_all, k)

@@ -107,6 +107,17 @@ cvs_status cvs_merge_lists(const float* scores, const int64_t* ids, int64_t list
                            int64_t len, int k, float* out_scores, int64_t* out_ids, void* stream);
 
 /*
+ * cvs_merge_lists with the lists anywhere in memory: list l's [b][len] scores
+ * start at scores + l * scores_list_stride (floats) and its ids at
+ * ids + l * ids_list_stride (int64); strides of at least b * len. Lets a caller
+ * gather each rank's scores and ids in ONE block per rank (one collective) and
+ * merge straight out of the gathered buffer. No counterpart in the reference.
+ */
+cvs_status cvs_merge_lists_strided(const float* scores, int64_t scores_list_stride, const int64_t* ids,
+                                   int64_t ids_list_stride, int64_t lists, int64_t b, int64_t len, int k,
+                                   float* out_scores, int64_t* out_ids, void* stream);
+
+/*
  * Same search as cvs_fused_topk, for callers that cannot allocate device
  * memory (a host application that owns the device-memory budget and forbids
  * plugins from calling cudaMalloc, a serving loop that cannot afford
