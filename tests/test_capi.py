@@ -70,6 +70,11 @@ def test_merge_and_ingest_contracts(lib):
     lib.cvs_merge_lists.argtypes = [vp, vp, i64, i64, i64, i32, vp, vp, vp]
     assert lib.cvs_merge_lists(None, None, 0, 4, 10, 5, None, None, None) == 1
     assert lib.cvs_merge_lists(None, None, 2, 4, 10, 0, None, None, None) == 1
+    lib.cvs_merge_lists_strided.argtypes = [vp, i64, vp, i64, i64, i64, i64, i32, vp, vp, vp]
+    # strides below b * len would overlap lists
+    assert lib.cvs_merge_lists_strided(16, 39, 16, 40, 2, 4, 10, 5, 16, 16, None) == 1
+    assert b"stride" in lib.cvs_last_error()
+    assert lib.cvs_merge_lists_strided(16, 40, 16, 40, 2, 4, 10, 2000, 16, 16, None) == 1  # k too large
     lib.cvs_ingest.argtypes = [vp, i32, i64, i32, i64, i32, i32, vp, vp]
     assert lib.cvs_ingest(None, 0, 0, 8, 8, 64, 1, None, None) == 0  # zero rows: nothing to do
     assert lib.cvs_ingest(None, 0, 5, 8, 8, 64, 1, None, None) == 1
