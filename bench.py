@@ -309,13 +309,20 @@ def run_ours(args, cfg):
     barrier()
     e2e_t0.record(stream)
     # Each step's results land in pinned host buffers (stream-ordered copies); the
-    # barrier after the loop waits for the last of them.
+    # barrier after the loop waits for the last of them. Step s's results are
+    # read back after step s+1 has been issued (a two-deep pipeline, as a serving
+    # loop would run it), so step s+1's query upload is not queued behind them.
     v_host = torch.empty((b, k), dtype=torch.float32, pin_memory=True)
     i_host = torch.empty((b, k), dtype=torch.int64, pin_memory=True)
+    prev = None
     for _ in range(args.steps):
-        v, i = index.search(q_host, k)
-        v_host.copy_(v, non_blocking=True)
-        i_host.copy_(i, non_blocking=True)
+        cur = index.search(q_host, k)
+        if prev is not None:
+            v_host.copy_(prev[0], non_blocking=True)
+            i_host.copy_(prev[1], non_blocking=True)
+        prev = cur
+    v_host.copy_(prev[0], non_blocking=True)
+    i_host.copy_(prev[1], non_blocking=True)
     e2e_t1.record(stream)
     barrier()
     host_t2 = time.time()

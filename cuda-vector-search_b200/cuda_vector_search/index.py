@@ -8,7 +8,10 @@ underneath:
 * storage: one ingest kernel converts to fp16, L2-normalises (cosine) and pads
   the width to a multiple of 64 in a single pass (index.py:35-41 + 27-32 there);
 * search: ``method="fused"`` (the default) runs the tcgen05 score + top-k kernel
-  (or the GEMV kernel for batches of at most 8) and a merge kernel;
+  (or the GEMV kernel for one or two queries) and a merge kernel; queries in
+  pinned host memory are copied on a side stream, so a caller that issues the
+  next search before reading back the previous results overlaps each upload
+  with the previous search;
 * there is no CPU storage and no fallback: a non-CUDA device or a GPU other than
   sm_100 raises RuntimeError. ``method="torch"`` (cuBLAS + topk) remains available
   on request, as in the reference.
@@ -32,6 +35,37 @@ _INGEST_CHUNK = 1 << 18  # rows staged per host->device copy
 METHODS = ("auto", "fused", "twopass", "torch")
 
 _KERNEL_DTYPES = (torch.float32, torch.float16, torch.bfloat16, torch.float64)
+
+_COPY_STREAMS: dict = {}  # device index -> side stream for host-to-device copies
+
+
+def _copy_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _COPY_STREAMS.get(idx)
+    if st is None:
+        st = _COPY_STREAMS[idx] = torch.cuda.Stream(device=idx)
+    return st
+
+
+def _upload_pinned(blk: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """Device copy of a pinned host block, made on a side stream.
+
+    The current stream waits for the copy (an event, no host synchronisation), so
+    the copy can run while the current stream's earlier kernels (the previous
+    search) still execute. The caller must not modify the pinned block until the
+    search is complete -- the same rule as for any non-blocking copy.
+    """
+    cur = torch.cuda.current_stream(device)
+    side = _copy_stream(device)
+    with torch.cuda.stream(side):
+        # Allocated on the side stream, so its memory is free of the side
+        # stream's earlier work; record_stream keeps it alive for the current
+        # stream's use.
+        dst = torch.empty(blk.shape, dtype=blk.dtype, device=device)
+        dst.copy_(blk, non_blocking=True)
+    cur.wait_stream(side)
+    dst.record_stream(cur)
+    return dst
 
 
 def _to_tensor(a) -> torch.Tensor:
@@ -68,7 +102,10 @@ def _ingest(src: torch.Tensor, device: torch.device, cosine: bool, out: torch.Te
     with torch.cuda.device(device):
         for start in range(0, n, _INGEST_CHUNK):
             blk = src[start : start + _INGEST_CHUNK]
-            blk_dev = blk.to(device, non_blocking=blk.is_pinned())
+            if blk.is_pinned() and blk.is_contiguous():
+                blk_dev = _upload_pinned(blk, device)
+            else:
+                blk_dev = blk.to(device, non_blocking=blk.is_pinned())
             if blk_dev.stride(1) != 1:
                 blk_dev = blk_dev.contiguous()
             mod.ingest_into(blk_dev, out[start : start + blk.shape[0]], cosine)

@@ -160,3 +160,19 @@ def test_plan_selects_gemv_only_for_one_or_two_queries(cvs, b, expect_gemv):
     v2, i2, plan2 = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, 10, 64)
     assert plan2.tolist()[0] == 64  # an explicit bq always selects tcgen05 tiles
     assert torch.equal(i, i2)
+
+
+def test_pinned_host_queries_back_to_back(cvs):
+    """Pinned host queries are uploaded on a side stream; several searches issued
+    back to back (no host synchronisation between them) must each see their own
+    queries and match the device-query results."""
+    x, q = _data(20000, 256, 300, seed=5)
+    index = cvs.Index(x.cuda(), metric="cosine")
+    parts = [q[i * 100:(i + 1) * 100] for i in range(3)]
+    ref = [index.search(p.cuda(), 10) for p in parts]
+    pinned = [p.float().pin_memory() for p in parts]
+    outs = [index.search(p, 10) for p in pinned]
+    torch.cuda.synchronize()
+    for (rv, ri), (v, i) in zip(ref, outs):
+        assert torch.equal(ri, i)
+        assert torch.allclose(rv, v, atol=0, rtol=0)
