@@ -13,6 +13,10 @@ step is a full sharded search (local fused top-k + NCCL all-gather + merge), and
 --impl reference times the reference's CPU path restated in numpy (oracle/,
 fp32 matmul + top-k with the reference's chunked merge) on the host cores, on a
 bounded sample of the same workload, scaled to the same unit.
+
+--sweep [--sweep-batches 1,8,256 --sweep-chunks 0,74 --report table.md] times the
+search over batch sizes and plan hints on one GPU instead (JSON rows + a
+markdown table with roofline fractions).
 """
 
 from __future__ import annotations
@@ -399,6 +403,74 @@ def run_ours(args, cfg):
         dist.destroy_process_group()
 
 
+def run_sweep(args, cfg):
+    """Plan sweep on one GPU (the reference's bench/sweep.py + report.py role):
+    for the config's corpus, every batch size in --sweep-batches and every plan
+    hint (bq 0 = automatic, 128 = one-CTA tiles, 256 = CTA pairs; chunks 0 =
+    one CTA (pair) per SM, or the given counts), the live CUDA-event time of the
+    search kernel and of the whole call. Prints one JSON row per point and a
+    markdown table; --report PATH also writes the table there."""
+    import torch
+
+    import cuda_vector_search as cvs
+    from cuda_vector_search import _ext
+
+    mod = _ext.load()
+    dev = torch.device("cuda", 0)
+    n, d, k = cfg["n"], cfg["d"], cfg["k"]
+    x = make_shard(torch, n, d, seed=1, first_chunk=0, device=dev)
+    index = cvs.Index(x, metric=cfg["metric"], device=dev, copy=False)
+    hbm_peak, tc_peak, _ = load_peaks()
+    d_pad = index._x.shape[1]
+    batches = [int(v) for v in args.sweep_batches.split(",")]
+    chunk_list = [int(v) for v in args.sweep_chunks.split(",")]
+    rows = []
+    for b in batches:
+        q = index._prep_queries(make_queries(torch, b, d, seed=2, device=dev))
+        for bq in (0, 128, 256):
+            if bq == 256 and b <= 128:
+                continue
+            for chunks in chunk_list:
+                for _ in range(3):
+                    mod.fused_topk(q, index._x, k, bq, chunks)
+                torch.cuda.synchronize()
+                reps = max(3, args.steps)
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+                for a_, b_ in evs:
+                    a_.record()
+                    b_.record()
+                t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                t0.record()
+                for a_, b_ in evs:
+                    mod.set_profile_events(a_.cuda_event, b_.cuda_event)
+                    _, _, plan = mod.fused_topk(q, index._x, k, bq, chunks)
+                t1.record()
+                torch.cuda.synchronize()
+                mod.set_profile_events(0, 0)
+                kern = sum(a_.elapsed_time(b_) for a_, b_ in evs) / reps
+                call = t0.elapsed_time(t1) / reps
+                tflops = 2.0 * b * n * d / (kern / 1e3) / 1e12
+                gbs = (2.0 * n * d_pad + 2.0 * b * d_pad + 12.0 * b * k) / (kern / 1e3) / 1e9
+                row = {"config": args.config, "n": n, "d": d, "b": b, "k": k, "bq": bq, "chunks": chunks,
+                       "plan": plan.tolist(), "kernel_ms": round(kern, 4), "call_ms": round(call, 4),
+                       "qps": round(b / (call / 1e3), 1), "tflops": round(tflops, 1), "gbs": round(gbs, 1),
+                       "tc_frac": round(tflops / tc_peak, 4), "hbm_frac": round(gbs / hbm_peak, 4)}
+                rows.append(row)
+                print(json.dumps(row), flush=True)
+    lines = [f"Plan sweep, {args.config}: {n} x {d} fp16, k={k}, {cfg['metric']} (one B200; kernel = CUDA events "
+             f"around the search kernel, call = whole fused_topk)", "",
+             "| b | bq hint | chunks | plan | kernel ms | call ms | QPS | TF/s | GB/s | TC frac | HBM frac |",
+             "|---|---|---|---|---|---|---|---|---|---|---|"]
+    for r in rows:
+        lines.append(f"| {r['b']} | {r['bq']} | {r['chunks']} | {r['plan']} | {r['kernel_ms']} | {r['call_ms']} | "
+                     f"{r['qps']:.0f} | {r['tflops']} | {r['gbs']} | {r['tc_frac']} | {r['hbm_frac']} |")
+    table = "\n".join(lines)
+    print(table)
+    if args.report:
+        Path(args.report).write_text(table + "\n")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -409,13 +481,19 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=0, help="override rows per GPU (profiling runs)")
     ap.add_argument("--batch", type=int, default=0, help="override the batch size (profiling runs)")
+    ap.add_argument("--sweep", action="store_true", help="plan sweep instead of the benchmark line")
+    ap.add_argument("--sweep-batches", default="1,2,8,32,128,256,512,1024")
+    ap.add_argument("--sweep-chunks", default="0")
+    ap.add_argument("--report", default="", help="with --sweep: write the markdown table to this path")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.rows:
         cfg["n"] = args.rows
     if args.batch:
         cfg["b"] = args.batch
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args, cfg)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_ours(args, cfg)

@@ -134,6 +134,8 @@ struct Plan {
   size_t bound_bytes = 0;  // per-query bounds, per-list tops and counts at the start of the workspace
   size_t clear_bytes = 0;  // the part of it cleared per call
   int rows_per_seg = 0;
+  int qpad_rows = 0;      // > 0: queries copied into a zero-padded workspace buffer of this many rows
+  size_t qpad_offset = 0; // its offset in the workspace
   size_t ws_bytes = 0;
 };
 
@@ -226,6 +228,16 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
   p->clear_bytes = static_cast<size_t>(b) * 4 * (1 + p->lists * (counted ? 2 : 1)) + 4 * static_cast<size_t>(p->qtiles);
   p->bound_bytes = round_up(p->clear_bytes, kWsAlign);
   p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
+  // Streamed queries are re-loaded for every corpus tile; rows of a partial query
+  // tile that lie outside the query matrix would be zero-filled by the TMA unit
+  // on every load, which costs up to a fifth of the kernel time at small
+  // batches. Such batches are copied into a zero-padded buffer of whole tiles.
+  const int tile_rows = p->pair ? 2 * kTcM : kTcM;
+  if (!p->qres && b % tile_rows != 0) {
+    p->qpad_rows = p->qtiles * tile_rows;
+    p->qpad_offset = p->ws_bytes;
+    p->ws_bytes += round_up(static_cast<size_t>(p->qpad_rows) * d_pad * 2, kWsAlign);
+  }
   return CVS_OK;
 }
 
@@ -307,7 +319,15 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   const bool prof = g_prof_start && g_prof_stop;
   cudaError_t e;
   // The shared per-query bounds must start at "none" (0) on every call.
-  if (p.clear_bytes && (e = clear_launch(bounds, round_up(p.clear_bytes, 4), s)) != cudaSuccess)
+  const void* q_tiles = q_f16;  // what the tensor map reads
+  if (p.qpad_rows > 0) {
+    void* qpad = static_cast<char*>(workspace) + p.qpad_offset;
+    if ((e = prepare_launch(bounds, round_up(p.clear_bytes, 4), q_f16, qpad, static_cast<int>(b), d_pad,
+                            p.qpad_rows, s)) != cudaSuccess)
+      return cuda_fail(e, "clearing the workspace and padding the queries");
+    q_tiles = qpad;
+  } else if (p.clear_bytes && (e = prepare_launch(bounds, round_up(p.clear_bytes, 4), nullptr, nullptr, 0,
+                                                   d_pad, 0, s)) != cudaSuccess)
     return cuda_fail(e, "clearing the per-query bounds");
   if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   if (p.gemv) {
@@ -327,7 +347,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     if ((e = gemv_launch(a, s)) != cudaSuccess) return cuda_fail(e, "gemv top-k launch");
   } else {
     CUtensorMap qmap, xmap;
-    if ((st = make_map(&qmap, q_f16, b, d_pad, kTcM)) != CVS_OK) return st;
+    if ((st = make_map(&qmap, q_tiles, p.qpad_rows > 0 ? p.qpad_rows : b, d_pad, kTcM)) != CVS_OK) return st;
     if ((st = make_map(&xmap, x_f16, n, d_pad, p.pair ? kTcN / 2 : kTcN)) != CVS_OK) return st;
     TcArgs a{};
     a.b = static_cast<int>(b);

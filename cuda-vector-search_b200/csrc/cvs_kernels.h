@@ -110,9 +110,11 @@ struct MergeKeysArgs {
 };
 cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream);
 
-// Zeroes `bytes` bytes at p (4-byte aligned) and lets the next kernel, launched
-// programmatically, start its prologue meanwhile.
-cudaError_t clear_launch(void* p, size_t bytes, cudaStream_t stream);
+// Zeroes `bytes` bytes at p (4-byte aligned); if q_dst is given, also copies the
+// b x d_pad fp16 queries q_src into q_dst and zeroes its rows b..rows_pad-1. Lets
+// the next kernel, launched programmatically, start its prologue meanwhile.
+cudaError_t prepare_launch(void* p, size_t bytes, const void* q_src, void* q_dst, int b, int d_pad,
+                           int rows_pad, cudaStream_t stream);
 
 // Launches `kernel` with programmatic stream serialisation: it may start while
 // the previous kernel on the stream finishes and must call

@@ -323,10 +323,16 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const Mer
 
 size_t merge_smem(int k) { return kMergeWarps * merge_warp_bytes(k); }
 
-__global__ void __launch_bounds__(256) clear_kernel(uint32_t* p, size_t words) {
+// Workspace preparation before a search: zeroes the cleared words and, for
+// padded query tiles, copies the queries (16-byte chunks) into the padded buffer
+// with zero rows after them.
+__global__ void __launch_bounds__(256) prepare_kernel(uint32_t* p, size_t words, const uint4* q_src, uint4* q_dst,
+                                                      size_t q_chunks, size_t pad_chunks) {
   grid_launch_dependents();
-  for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < words; i += static_cast<size_t>(gridDim.x) * 256)
-    p[i] = 0u;
+  const size_t stride = static_cast<size_t>(gridDim.x) * 256;
+  for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < words; i += stride) p[i] = 0u;
+  for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < pad_chunks; i += stride)
+    q_dst[i] = i < q_chunks ? q_src[i] : make_uint4(0u, 0u, 0u, 0u);
 }
 
 }  // namespace
@@ -345,11 +351,17 @@ cudaError_t merge_keys_launch(const MergeKeysArgs& a, cudaStream_t stream) {
                              stream, a);
 }
 
-cudaError_t clear_launch(void* p, size_t bytes, cudaStream_t stream) {
+cudaError_t prepare_launch(void* p, size_t bytes, const void* q_src, void* q_dst, int b, int d_pad,
+                           int rows_pad, cudaStream_t stream) {
   const size_t words = bytes / 4;
-  if (words == 0) return cudaSuccess;
-  const unsigned grid = static_cast<unsigned>(std::min<size_t>((words + 255) / 256, 1024));
-  clear_kernel<<<grid, 256, 0, stream>>>(static_cast<uint32_t*>(p), words);
+  const size_t row_chunks = static_cast<size_t>(d_pad) / 8;  // 16-byte chunks per fp16 row
+  const size_t q_chunks = q_dst ? static_cast<size_t>(b) * row_chunks : 0;
+  const size_t pad_chunks = q_dst ? static_cast<size_t>(rows_pad) * row_chunks : 0;
+  const size_t work = std::max(words, pad_chunks);
+  if (work == 0) return cudaSuccess;
+  const unsigned grid = static_cast<unsigned>(std::min<size_t>((work + 255) / 256, 1024));
+  prepare_kernel<<<grid, 256, 0, stream>>>(static_cast<uint32_t*>(p), words, static_cast<const uint4*>(q_src),
+                                           static_cast<uint4*>(q_dst), q_chunks, pad_chunks);
   return cudaGetLastError();
 }
 
