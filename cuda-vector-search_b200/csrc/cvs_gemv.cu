@@ -1,7 +1,8 @@
-// CUDA-core GEMV + top-k for one or two queries (k <= 32): the HBM-bound case.
-// From three queries on, the per-row arithmetic of this kernel exceeds the
-// corpus stream and the tcgen05 kernel is faster. Replaces the reference's fused kernel at bq=16 for tiny batches
-// (cuda_vector_search/csrc/kernels.cu:313-371 run with nq <= 2, where 14 of
+// CUDA-core GEMV + top-k for a single query (k <= 32): the HBM-bound case.
+// From two queries on, the tcgen05 kernel (with padded query tiles) streams the
+// corpus at least as fast, and from three on this kernel's per-row arithmetic
+// exceeds the stream. Replaces the reference's fused kernel at bq=16 for tiny batches
+// (cuda_vector_search/csrc/kernels.cu:313-371 run with nq = 1, where 15 of
 // its 16 query rows are padding).
 //
 // Each warp owns whole corpus rows: lane l reads 16-byte chunks l, l+32, ... of
@@ -201,9 +202,9 @@ GemvKernel kernel_nq(int d_pad) {
   }
 }
 
-// The instantiation for b (1 or 2) queries of width d_pad; CPL = 16-byte chunks
-// per lane per row.
-GemvKernel select_kernel(int b, int d_pad) { return b == 1 ? kernel_nq<1>(d_pad) : kernel_nq<2>(d_pad); }
+// The instantiation for one query of width d_pad; CPL = 16-byte chunks per lane
+// per row.
+GemvKernel select_kernel(int, int d_pad) { return kernel_nq<1>(d_pad); }
 
 }  // namespace
 

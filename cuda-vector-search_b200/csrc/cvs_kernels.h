@@ -66,10 +66,10 @@ int tc_pair_max_clusters(int epi, bool resident_queries, int ksl);
 cudaError_t tc_pair_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                            const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
 
-// ---- CUDA-core GEMV + top-k for batches of one or two queries --------------
+// ---- CUDA-core GEMV + top-k for a single query ------------------------------
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxK = 32;
-constexpr int kGemvMaxBatch = 2;  // queries per GEMV launch (the tcgen05 kernel is faster beyond)
+constexpr int kGemvMaxBatch = 1;  // queries per GEMV launch (the tcgen05 kernel is as fast beyond)
 
 struct GemvArgs {
   const __half* x;    // [n][d_pad]

@@ -26,7 +26,7 @@ constexpr int kMergeMaxK = 1024;
 constexpr int kKeysThreads = 256;     // one CTA (8 warps) per query in the key merge
 constexpr int kKeysWarps = kKeysThreads / 32;
 constexpr int kKeysBatch = 8;         // keys in flight per lane
-constexpr int kMergeTopsPerLane = 16;  // up to 512 lists per query
+constexpr int kMergeTopsPerLane = 32;  // up to 1024 lists per query
 
 // Shared memory per warp of the list merge: radix histogram, k selected keys.
 __host__ __device__ constexpr size_t merge_warp_bytes(int k) {

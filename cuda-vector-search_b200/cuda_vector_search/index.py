@@ -8,7 +8,7 @@ underneath:
 * storage: one ingest kernel converts to fp16, L2-normalises (cosine) and pads
   the width to a multiple of 64 in a single pass (index.py:35-41 + 27-32 there);
 * search: ``method="fused"`` (the default) runs the tcgen05 score + top-k kernel
-  (or the GEMV kernel for one or two queries) and a merge kernel; queries in
+  (or the GEMV kernel for a single query) and a merge kernel; queries in
   pinned host memory are copied on a side stream, so a caller that issues the
   next search before reading back the previous results overlaps each upload
   with the previous search;
@@ -181,7 +181,7 @@ class Index:
         """Return (scores [b, k] float32, ids [b, k] int64), best first.
 
         method:
-            "fused"   - tcgen05 (or GEMV for b <= 2) scores + top-k in one pass (k <= 1024)
+            "fused"   - tcgen05 (or GEMV for b = 1) scores + top-k in one pass (k <= 1024)
             "twopass" - score kernel writes the full matrix, then torch.topk
             "torch"   - torch.matmul (cuBLAS) + torch.topk
             "auto"    - fused when k <= 1024, else twopass

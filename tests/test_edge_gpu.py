@@ -149,8 +149,8 @@ def test_dry_tile_regimes(cvs, chunks, b, k):
     _check(cvs, x, q, k, chunks=chunks if chunks else None)
 
 
-@pytest.mark.parametrize("b,expect_gemv", [(1, True), (2, True), (3, False), (8, False)])
-def test_plan_selects_gemv_only_for_one_or_two_queries(cvs, b, expect_gemv):
+@pytest.mark.parametrize("b,expect_gemv", [(1, True), (2, False), (3, False), (8, False)])
+def test_plan_selects_gemv_only_for_one_query(cvs, b, expect_gemv):
     from cuda_vector_search import _ext
 
     x, q = _data(5000, 256, b, seed=b)
