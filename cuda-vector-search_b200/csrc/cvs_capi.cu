@@ -222,9 +222,13 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
   }
   plan_tc_grid(p, b, n, dev.sms, chunks, p->epi, d_pad, bq);
   p->lists = p->segs * tc_lists_per_segment(p->epi);
+  // Buffer lists track their published rank in registers: 4 ranks when that
+  // rank is enough for the lists at hand, 8 when there are too few lists
+  // (large batches share the SMs among more query tiles).
+  if (p->epi == kEpiTopkBuf && tops_j(k, p->lists, 8) > 4 && tops_j(k, p->lists, 8) <= 8) p->epi = kEpiTopkBuf8;
   // Per-query shared bound, per-list published scores, (buffer lists) per-list
   // key counts and the per-query-tile tile counters, all cleared per call.
-  const bool counted = p->epi == kEpiTopkBuf;
+  const bool counted = is_buf_epi(p->epi);
   p->clear_bytes = static_cast<size_t>(b) * 4 * (1 + p->lists * (counted ? 2 : 1)) + 4 * static_cast<size_t>(p->qtiles);
   p->bound_bytes = round_up(p->clear_bytes, kWsAlign);
   p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
@@ -363,8 +367,8 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     a.part = part;
     a.gthr = bounds;
     a.tops = bounds + b;
-    const size_t list_words = static_cast<size_t>(b) * p.lists * (p.epi == kEpiTopkBuf ? 2 : 1);
-    a.counts = p.epi == kEpiTopkBuf ? reinterpret_cast<int*>(bounds + b + static_cast<size_t>(b) * p.lists) : nullptr;
+    const size_t list_words = static_cast<size_t>(b) * p.lists * (is_buf_epi(p.epi) ? 2 : 1);
+    a.counts = is_buf_epi(p.epi) ? reinterpret_cast<int*>(bounds + b + static_cast<size_t>(b) * p.lists) : nullptr;
     // Tiles are claimed at run time; a.segs CTAs (pairs) per query tile share them.
     a.tile_counter = reinterpret_cast<int*>(bounds + b + list_words);
     // Two dry tiles whenever a CTA can expect three or more tiles, one for two:
@@ -385,7 +389,7 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   m.stride = p.cap;
   m.per_list = k;
   // Buffer lists end with up to cap keys each; their counts follow the tops.
-  m.counts = (!p.gemv && p.epi == kEpiTopkBuf)
+  m.counts = (!p.gemv && is_buf_epi(p.epi))
                  ? reinterpret_cast<const int*>(bounds + b + static_cast<size_t>(b) * p.lists)
                  : nullptr;
   m.k = k;
@@ -394,13 +398,8 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   m.tops = bounds + b;
   m.tops_n = p.lists;
   // Register lists and GEMV CTAs publish their best score (m = k lists needed);
-  // buffer lists publish their J-th best with J = ceil(2k / lists) (m = ceil(k / J)).
-  if (!p.gemv && p.epi == kEpiTopkBuf) {
-    const int j = std::min(k, std::max(1, (2 * k + p.lists - 1) / p.lists));
-    m.tops_m = (k + j - 1) / j;
-  } else {
-    m.tops_m = k;
-  }
+  // buffer lists publish their J-th best (m = tops_m lists needed).
+  m.tops_m = (!p.gemv && is_buf_epi(p.epi)) ? tops_m(k, p.lists, buf_reg_ranks(p.epi)) : k;
   m.out_v = out_scores;
   m.out_i = reinterpret_cast<long long*>(out_ids);
   m.err = dev.err;

@@ -229,32 +229,20 @@ struct EpiTopkReg {
   }
 };
 
-// Rank of the per-list value a list publishes (its J-th best) and how many lists
-// must reach a value for it to bound the query's k-th best (m lists x J rows
-// >= k rows). With at least 2k lists this is (1, k): every list publishes its
-// best. The merge uses the same pair.
-__host__ __device__ __forceinline__ int tops_j(int k, int lists) {
-  const int j = (2 * k + lists - 1) / max(1, lists);
-  return j < 1 ? 1 : (j > k ? k : j);
-}
-__host__ __device__ __forceinline__ int tops_m(int k, int lists) {
-  const int j = tops_j(k, lists);
-  return (k + j - 1) / j;
-}
-
 // Per-query candidate buffer of `cap` keys in global memory (L2 resident) for
 // k > 32. A key is appended when its score beats the list's k-th best (as of
 // its last compaction) and the query's shared bound; when a list could
 // overflow on the next chunk, the warp loads it into shared memory in one round
 // trip, radix-selects its top k and J-th best there, writes the top k back and
 // publishes the J-th best for the query's bound.
+template <int RJ>
 struct EpiTopkBuf {
   // Two column stripes per TMEM quadrant, as the register lists.
   static constexpr int kSubs = 2;
   static constexpr bool kTops = true;
   static constexpr int kScratchKeys = 512;  // shared-memory compaction up to cap 512 (k <= 256)
-  static constexpr int kRegJ = 4;           // J-th best tracked in registers for J <= kRegJ
-  static __device__ __forceinline__ int jrank(int k, int lists) { return tops_j(k, lists); }
+  static constexpr int kRegJ = RJ;  // J-th best tracked in registers for J <= kRegJ
+  static __device__ __forceinline__ int jrank(int k, int lists) { return tops_j(k, lists, RJ); }
   uint64_t* list;
   int cnt;
   int jr;           // J: rank of the value this list publishes
@@ -269,7 +257,7 @@ struct EpiTopkBuf {
   __device__ __forceinline__ void init(const TcArgs& a) {
     list = nullptr;
     cnt = 0;
-    jr = tops_j(a.k, a.segs * kSubs);
+    jr = tops_j(a.k, a.segs * kSubs, RJ);
     thr = -INFINITY;
     bound = -INFINITY;
     best = -INFINITY;
@@ -370,12 +358,18 @@ struct EpiTopkBuf {
   }
 
   // Dry tiles need the J-th best in registers.
-  static __device__ __forceinline__ bool dry_ok(const TcArgs& a) { return tops_j(a.k, a.segs * kSubs) <= kRegJ; }
+  static __device__ __forceinline__ bool dry_ok(const TcArgs& a) { return tops_j(a.k, a.segs * kSubs, RJ) <= kRegJ; }
   __device__ __forceinline__ void dry(const uint32_t (&r)[32], int nvalid, bool qvalid) {
     if (!qvalid) return;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nvalid) track(__uint_as_float(r[j]));
+    // Only scores that beat the kRegJ-th tracked one can change tj.
+    const float lo = tj[kRegJ - 1];
+    if (!(max_valid(r, nvalid) > lo)) return;
+    uint32_t m = above_mask(r, lo, nvalid);
+    while (m) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      track(pick(r, j));
+    }
   }
 
   // The list's segment holds at least J rows scoring >= best (the value is the
@@ -453,6 +447,11 @@ struct EpiStore {
     }
   }
 };
+
+template <class E>
+struct is_buf : std::false_type {};
+template <int RJ>
+struct is_buf<EpiTopkBuf<RJ>> : std::true_type {};
 
 template <class E>
 struct is_store : std::false_type {};

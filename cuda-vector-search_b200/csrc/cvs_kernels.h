@@ -26,7 +26,32 @@ enum TcEpilogue : int {
   kEpiTopkBuf = 2,     // k  > 32: per-query candidate buffer in global memory
   kEpiStoreF32 = 3,    // write the score matrix as fp32
   kEpiStoreF16 = 4,    // write the score matrix as fp16
+  kEpiTopkBuf8 = 5,    // k > 32 with fewer lists: candidate buffers, 8 ranks tracked in registers
 };
+
+// Rank J of the per-list value a buffer list (k > 32) publishes (its J-th best)
+// and how many lists m must reach a value for it to bound the query's k-th best
+// (m lists x J rows >= k rows). Aim: J = ceil(2k / lists), so m is about half
+// the lists; but J is held to regj (the ranks the epilogue tracks in registers,
+// which is what lets it publish from the first tile on) whenever m = ceil(k / J)
+// still fits in the lists. The merge uses the same pair.
+__host__ __device__ inline int tops_j(int k, int lists, int regj) {
+  lists = lists < 1 ? 1 : lists;
+  int j = (2 * k + lists - 1) / lists;
+  const int jmin = (k + lists - 1) / lists;  // smallest J with m <= lists
+  if (j > regj) j = jmin > regj ? jmin : regj;
+  return j < 1 ? 1 : (j > k ? k : j);
+}
+__host__ __device__ inline int tops_m(int k, int lists, int regj) {
+  const int j = tops_j(k, lists, regj);
+  return (k + j - 1) / j;
+}
+
+// Ranks a buffer epilogue tracks in registers (kEpiTopkBuf: 4, kEpiTopkBuf8: 8;
+// more ranks cost registers in the drain loop, so 8 only where 4 cannot serve).
+__host__ __device__ inline int buf_reg_ranks(int epi) { return epi == kEpiTopkBuf8 ? 8 : 4; }
+__host__ __device__ inline bool is_buf_epi(int epi) { return epi == kEpiTopkBuf || epi == kEpiTopkBuf8; }
+
 
 struct TcArgs {
   int b;              // queries

@@ -273,7 +273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     Epi epi;
     epi.init(a);
-    if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
+    if constexpr (is_buf<Epi>::value) {
       if (qvalid)
         epi.list = a.part + (static_cast<size_t>(q) * a.segs * Epi::kSubs + seg * Epi::kSubs + sub) * a.cap;
     }
@@ -310,7 +310,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
       }
       const int row0 = static_cast<int>(v & kLogTileMask) * kTcN;
       const int valid = min(kTcN, a.n - row0);
-      if constexpr (std::is_same<Epi, EpiTopkBuf>::value) epi.redo = (v & kLogRedo) != 0;
+      if constexpr (is_buf<Epi>::value) epi.redo = (v & kLogRedo) != 0;
       for (int c = sub * kChunks; c < (sub + 1) * kChunks; ++c) {
         if (c * 32 >= valid) break;
         uint32_t r[32];
@@ -323,7 +323,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
           epi.dry(r, nv, qvalid);
         } else {
           epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
-          if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
+          if constexpr (is_buf<Epi>::value) {
             epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a,
                               Epi::jrank(a.k, a.segs * Epi::kSubs), sh.hist(ew),
                               sh.scratch(ew, Epi::kScratchKeys), lane);
@@ -424,7 +424,8 @@ cudaError_t pair_launch_epi(int epi, const CUtensorMap* qmap, const CUtensorMap*
   switch (epi) {
     case kEpiTopkReg16: return pair_launch_one<QRES, EpiTopkReg<16>>(qmap, xmap, a, stream);
     case kEpiTopkReg32: return pair_launch_one<QRES, EpiTopkReg<32>>(qmap, xmap, a, stream);
-    case kEpiTopkBuf: return pair_launch_one<QRES, EpiTopkBuf>(qmap, xmap, a, stream);
+    case kEpiTopkBuf: return pair_launch_one<QRES, EpiTopkBuf<4>>(qmap, xmap, a, stream);
+    case kEpiTopkBuf8: return pair_launch_one<QRES, EpiTopkBuf<8>>(qmap, xmap, a, stream);
     case kEpiStoreF32: return pair_launch_one<QRES, EpiStore<true>>(qmap, xmap, a, stream);
     case kEpiStoreF16: return pair_launch_one<QRES, EpiStore<false>>(qmap, xmap, a, stream);
     default: return cudaErrorInvalidValue;
@@ -436,7 +437,8 @@ int pair_clusters_epi(int epi, int ksl) {
   switch (epi) {
     case kEpiTopkReg16: return pair_clusters_one<QRES, EpiTopkReg<16>>(ksl);
     case kEpiTopkReg32: return pair_clusters_one<QRES, EpiTopkReg<32>>(ksl);
-    case kEpiTopkBuf: return pair_clusters_one<QRES, EpiTopkBuf>(ksl);
+    case kEpiTopkBuf: return pair_clusters_one<QRES, EpiTopkBuf<4>>(ksl);
+    case kEpiTopkBuf8: return pair_clusters_one<QRES, EpiTopkBuf<8>>(ksl);
     case kEpiStoreF32: return pair_clusters_one<QRES, EpiStore<true>>(ksl);
     case kEpiStoreF16: return pair_clusters_one<QRES, EpiStore<false>>(ksl);
     default: return 0;
@@ -446,8 +448,8 @@ int pair_clusters_epi(int epi, int ksl) {
 }  // namespace
 
 bool tc_pair_resident_queries(int epi, int ksl) {
-  const int subs = epi == kEpiTopkBuf ? EpiTopkBuf::kSubs : 2;
-  const int scratch = epi == kEpiTopkBuf ? EpiTopkBuf::kScratchKeys : 0;
+  const int subs = is_buf_epi(epi) ? EpiTopkBuf<4>::kSubs : 2;
+  const int scratch = is_buf_epi(epi) ? EpiTopkBuf<4>::kScratchKeys : 0;
   return static_cast<size_t>(pair_layout(true, ksl, subs, scratch).total) + 1024 <= 232448;
 }
 

@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     Epi epi;
     epi.init(a);
-    if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
+    if constexpr (is_buf<Epi>::value) {
       if (qvalid)
         epi.list = a.part + (static_cast<size_t>(q) * a.segs * Epi::kSubs + seg * Epi::kSubs + sub) * a.cap;
     }
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
       }
       const int row0 = static_cast<int>(v & kLogTileMask) * kTcN;
       const int valid = min(kTcN, a.n - row0);
-      if constexpr (std::is_same<Epi, EpiTopkBuf>::value) epi.redo = (v & kLogRedo) != 0;
+      if constexpr (is_buf<Epi>::value) epi.redo = (v & kLogRedo) != 0;
       for (int c = sub * kChunks; c < (sub + 1) * kChunks; ++c) {
         if (c * 32 >= valid) break;
         uint32_t r[32];
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
           epi.dry(r, nv, qvalid);
         } else {
           epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
-          if constexpr (std::is_same<Epi, EpiTopkBuf>::value) {
+          if constexpr (is_buf<Epi>::value) {
             epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a,
                               Epi::jrank(a.k, a.segs * Epi::kSubs), sh.hist(ew),
                               sh.scratch(ew, Epi::kScratchKeys), lane);
@@ -373,7 +373,8 @@ cudaError_t launch_epi(int epi, const CUtensorMap* qmap, const CUtensorMap* xmap
   switch (epi) {
     case kEpiTopkReg16: return launch_one<QRES, EpiTopkReg<16>>(qmap, xmap, a, stream);
     case kEpiTopkReg32: return launch_one<QRES, EpiTopkReg<32>>(qmap, xmap, a, stream);
-    case kEpiTopkBuf: return launch_one<QRES, EpiTopkBuf>(qmap, xmap, a, stream);
+    case kEpiTopkBuf: return launch_one<QRES, EpiTopkBuf<4>>(qmap, xmap, a, stream);
+    case kEpiTopkBuf8: return launch_one<QRES, EpiTopkBuf<8>>(qmap, xmap, a, stream);
     case kEpiStoreF32: return launch_one<QRES, EpiStore<true>>(qmap, xmap, a, stream);
     case kEpiStoreF16: return launch_one<QRES, EpiStore<false>>(qmap, xmap, a, stream);
     default: return cudaErrorInvalidValue;
@@ -384,8 +385,8 @@ cudaError_t launch_epi(int epi, const CUtensorMap* qmap, const CUtensorMap* xmap
 
 bool tc_resident_queries(int epi, int ksl) {
   if (ksl > kTcMaxResidentSlices) return false;
-  const int subs = epi == kEpiTopkBuf ? EpiTopkBuf::kSubs : 2;
-  const int scratch = epi == kEpiTopkBuf ? EpiTopkBuf::kScratchKeys : 0;
+  const int subs = is_buf_epi(epi) ? EpiTopkBuf<4>::kSubs : 2;
+  const int scratch = is_buf_epi(epi) ? EpiTopkBuf<4>::kScratchKeys : 0;
   return static_cast<size_t>(make_layout(true, ksl, subs, scratch).total) + 1024 <= 232448;
 }
 
@@ -393,7 +394,8 @@ int tc_lists_per_segment(int epi) {
   switch (epi) {
     case kEpiTopkReg16: return EpiTopkReg<16>::kSubs;
     case kEpiTopkReg32: return EpiTopkReg<32>::kSubs;
-    case kEpiTopkBuf: return EpiTopkBuf::kSubs;
+    case kEpiTopkBuf:
+    case kEpiTopkBuf8: return EpiTopkBuf<4>::kSubs;
     default: return 1;
   }
 }
