@@ -17,7 +17,8 @@ constexpr int kTcN = 256;          // corpus rows per tile (MMA N; TMEM columns)
 constexpr int kTcK = 64;           // halves per K slice (one 128-byte swizzled row)
 constexpr int kTcStages = 4;
 constexpr int kTcMaxResidentSlices = 7;  // queries stay in smem when d_pad <= 448
-// Dry tiles of the top-k epilogues (see cvs_epilogue.cuh): at most this many.
+// Dry tiles of the top-k epilogues (see cvs_epilogue.cuh): at most this many
+// (TileSource in cvs_sched.cuh keeps two).
 constexpr int kDryTiles = 2;
 
 enum TcEpilogue : int {

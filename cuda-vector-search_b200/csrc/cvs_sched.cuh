@@ -16,7 +16,7 @@
 // TMEM accumulators let it, that is after every role of both CTAs has started
 // iteration i - 9 or later (six stages, two accumulators).
 //
-// Dry tiles (see kDryTiles in cvs_epilogue.cuh) fit in as follows: the first
+// Dry tiles (cvs_epilogue.cuh; at most kDryTiles, cvs_kernels.h) fit in as follows: the first
 // `dry` tiles a CTA claims are logged as dry, and once the counter runs out
 // they are logged again, as redo iterations, before the end marker.
 #pragma once
@@ -94,7 +94,8 @@ struct TileSource {
   int dry;      // leading tiles read dry and revisited at the end
   int claimed;  // tiles handed out so far (excluding redo)
   int redo;     // dry tiles revisited so far
-  int first[2];
+  int first0;   // the dry tiles, revisited at the end (kDryTiles <= 2);
+  int first1;   // scalars rather than an array so they stay in registers
 
   __device__ __forceinline__ void init(int* c, int n, int begin, int end, int d) {
     counter = c;
@@ -104,7 +105,7 @@ struct TileSource {
     dry = d;
     claimed = 0;
     redo = 0;
-    first[0] = first[1] = 0;
+    first0 = first1 = 0;
   }
 
   // Value for the next log entry.
@@ -120,7 +121,8 @@ struct TileSource {
       if (t >= 0) {
         uint32_t v = static_cast<uint32_t>(t);
         if (claimed < dry) {
-          first[claimed] = t;
+          if (claimed == 0) first0 = t;
+          else first1 = t;
           v |= kLogDry;
         }
         ++claimed;
@@ -128,7 +130,11 @@ struct TileSource {
       }
     }
     const int nd = claimed < dry ? claimed : dry;
-    if (redo < nd) return static_cast<uint32_t>(first[redo++]) | kLogRedo;
+    if (redo < nd) {
+      const int t = redo == 0 ? first0 : first1;
+      ++redo;
+      return static_cast<uint32_t>(t) | kLogRedo;
+    }
     redo = nd + 1;  // stays exhausted
     return kLogEnd;
   }
