@@ -37,6 +37,7 @@ METHODS = ("auto", "fused", "twopass", "torch")
 _KERNEL_DTYPES = (torch.float32, torch.float16, torch.bfloat16, torch.float64)
 
 _COPY_STREAMS: dict = {}  # device index -> side stream for host-to-device copies
+_SIDE_UPLOAD_BYTES = 256 << 10  # smaller pinned uploads stay on the current stream
 
 
 def _copy_stream(device: torch.device) -> torch.cuda.Stream:
@@ -98,17 +99,20 @@ def _ingest(src: torch.Tensor, device: torch.device, cosine: bool, out: torch.Te
         mod.ingest_into(src, out, cosine)
         return out
     # Host source: stage fixed-size row blocks so a huge array never needs a
-    # second full-size copy on either side.
+    # second full-size copy on either side. Pinned blocks of at least
+    # _SIDE_UPLOAD_BYTES go through the side stream (the extra host work of the
+    # stream switch outweighs the overlap for small ones).
+    pinned = src.is_pinned()
     with torch.cuda.device(device):
         for start in range(0, n, _INGEST_CHUNK):
-            blk = src[start : start + _INGEST_CHUNK]
-            if blk.is_pinned() and blk.is_contiguous():
+            blk = src if n <= _INGEST_CHUNK else src[start : start + _INGEST_CHUNK]
+            if pinned and blk.nbytes >= _SIDE_UPLOAD_BYTES and blk.is_contiguous():
                 blk_dev = _upload_pinned(blk, device)
             else:
-                blk_dev = blk.to(device, non_blocking=blk.is_pinned())
+                blk_dev = blk.to(device, non_blocking=pinned)
             if blk_dev.stride(1) != 1:
                 blk_dev = blk_dev.contiguous()
-            mod.ingest_into(blk_dev, out[start : start + blk.shape[0]], cosine)
+            mod.ingest_into(blk_dev, out if n <= _INGEST_CHUNK else out[start : start + blk.shape[0]], cosine)
     return out
 
 
