@@ -38,7 +38,7 @@ def test_oracle_matches_reference(case):
         # torch's CPU norm is not correctly rounded, so a few elements of the
         # reference's normalised rows differ by one fp16 ulp from this
         # restatement (test_normalize_matches_torch_reference_formula bounds it);
-        # scores then move by ~1e-5, so near-ties are judged at 1e-4 here.
+        # scores then move by ~1e-5, so near-ties are compared at 1e-4 here.
         x, q = normalize_rows_fp16(x), normalize_rows_fp16(q)
         rel = 1e-4
     k = min(case["k"], case["n"])
