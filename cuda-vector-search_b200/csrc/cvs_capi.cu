@@ -166,7 +166,12 @@ int pair_clusters(int epi, bool qres, int ksl, int sms) {
 void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks, int epi, int d_pad, int bq = 0) {
   const int ksl = d_pad / kTcK;
   // bq hint: 16..128 keeps 128-query tiles on one CTA, 256 asks for CTA pairs.
-  p->pair = bq > 0 ? (bq > kTcM && b > kTcM) : (b > kTcM);
+  // Automatic: CTA pairs for more than 128 queries unless their 256-query tiles
+  // would pad more rows than 128-query tiles (b = 300: 512 against 384 rows;
+  // measured 20-30% slower), since every padded row costs MMA work.
+  const int64_t pair_rows = (b + 2 * kTcM - 1) / (2 * kTcM) * (2 * kTcM);
+  const int64_t cta_rows = (b + kTcM - 1) / kTcM * kTcM;
+  p->pair = bq > 0 ? (bq > kTcM && b > kTcM) : (b > kTcM && pair_rows == cta_rows);
   p->ntiles = static_cast<int>((n + kTcN - 1) / kTcN);
   int slots;
   if (p->pair) {

@@ -176,3 +176,16 @@ def test_pinned_host_queries_back_to_back(cvs):
     for (rv, ri), (v, i) in zip(ref, outs):
         assert torch.equal(ri, i)
         assert torch.allclose(rv, v, atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("b,tile", [(200, 256), (256, 256), (300, 128), (384, 128), (512, 256), (640, 128)])
+def test_plan_prefers_the_tile_with_fewer_padded_rows(cvs, b, tile):
+    """CTA pairs (256-query tiles) unless 128-query tiles pad fewer rows; results
+    are the oracle's either way."""
+    from cuda_vector_search import _ext
+
+    x, q = _data(6000, 128, b, seed=b + 7)
+    index = cvs.Index(x.cuda(), metric="ip")
+    v, i, plan = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, 10)
+    assert plan.tolist()[0] == tile
+    _check(cvs, x, q, 10)
