@@ -272,6 +272,19 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
     if (warp == 0) select_and_emit(all, m, a.k, a.id_offset, hist, sel, out_v, out_i, lane);
     return;
   }
+  if (cnt <= 32 && a.k <= 32) {
+    // Typical for small k (the bound leaves a few dozen keys at most): warp 0
+    // ranks the survivors against each other directly.
+    if (warp == 0) {
+      const uint64_t key = lane < cnt ? surv[lane] : 0ull;
+      int rank = 0;
+#pragma unroll
+      for (int t = 0; t < 32; ++t) rank += shfl_u64(key, t) > key ? 1 : 0;
+      if (lane < cnt && rank < a.k) emit_key(key, rank, a.id_offset, out_v, out_i);
+      for (int j = cnt + lane; j < a.k; j += 32) emit_key(0ull, j, a.id_offset, out_v, out_i);
+    }
+    return;
+  }
   // k-th best survivor (warp 0), then the winners (keys are unique, so exactly
   // min(k, cnt) survivors are >= it).
   if (warp == 0) {

@@ -367,6 +367,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
     }
   }
 
+  // This CTA's results are written (or it is leaving on an error): the merge,
+  // launched programmatically, may be scheduled as CTAs finish; it still waits
+  // for the whole grid before reading.
+  grid_launch_dependents();
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // neither CTA releases TMEM or leaves while the other still works

@@ -346,6 +346,10 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     }
   }
 
+  // This CTA's results are written (or it is leaving on an error): the merge,
+  // launched programmatically, may be scheduled as CTAs finish; it still waits
+  // for the whole grid before reading.
+  grid_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
