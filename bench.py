@@ -206,9 +206,9 @@ class ClockSampler:
         except Exception:  # nvidia-smi missing: report no clocks
             self.proc = None
 
-    def stop(self, window=None):
-        """Summary of the samples taken inside `window` = (start, end) host times
-        (time.time()) of the timed region; all samples if fewer than 3 fall in it."""
+    def stop(self, windows=None):
+        """Summary of the samples taken inside `windows` = [(start, end), ...] host
+        times (time.time()) of the timed loops; all samples if fewer than 3 fall in them."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.1)
@@ -227,8 +227,8 @@ class ClockSampler:
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         inside = rows
-        if window is not None:
-            sel = [r for r in rows if r[0] is not None and window[0] <= r[0] <= window[1]]
+        if windows:
+            sel = [r for r in rows if r[0] is not None and any(w0 <= r[0] <= w1 for w0, w1 in windows)]
             inside = sel if len(sel) >= 3 else rows
         sm = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
         mx = [float(r[3]) for r in inside if r[3].replace(".", "").isdigit()]
@@ -309,30 +309,42 @@ def run_ours(args, cfg):
     kern_ms = [a.elapsed_time(bb) for a, bb in ev_pairs]
 
     # End to end through the public API: pinned host fp32 queries in, host results out.
-    e2e_t0, e2e_t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    e2e_t0.record(stream)
+    # It starts from the same rested state as the loop above: after ~200 ms of
+    # back-to-back searches the 1 kW power cap lowers the SM clock, and without
+    # the pause this loop would run in that window while the first did not.
     # Each step's results land in pinned host buffers (stream-ordered copies); the
     # barrier after the loop waits for the last of them. Step s's results are
     # read back after step s+1 has been issued (a two-deep pipeline, as a serving
     # loop would run it), so step s+1's query upload is not queued behind them.
+    # The pinned result buffers are allocated, and the path warmed up (side copy
+    # stream, allocator blocks), before the timed loop: a pinned allocation
+    # (cudaHostAlloc) takes milliseconds and leaves the GPU idle meanwhile.
     v_host = torch.empty((b, k), dtype=torch.float32, pin_memory=True)
     i_host = torch.empty((b, k), dtype=torch.int64, pin_memory=True)
-    prev = None
-    for _ in range(args.steps):
-        cur = index.search(q_host, k)
-        if prev is not None:
-            v_host.copy_(prev[0], non_blocking=True)
-            i_host.copy_(prev[1], non_blocking=True)
-        prev = cur
-    v_host.copy_(prev[0], non_blocking=True)
-    i_host.copy_(prev[1], non_blocking=True)
+
+    def e2e_loop(steps):
+        prev = None
+        for _ in range(steps):
+            cur = index.search(q_host, k)
+            if prev is not None:
+                v_host.copy_(prev[0], non_blocking=True)
+                i_host.copy_(prev[1], non_blocking=True)
+            prev = cur
+        v_host.copy_(prev[0], non_blocking=True)
+        i_host.copy_(prev[1], non_blocking=True)
+
+    e2e_loop(max(args.warmup, 3))
+    e2e_t0, e2e_t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    time.sleep(0.3)
+    barrier()
+    host_e0 = time.time()
+    e2e_t0.record(stream)
+    e2e_loop(args.steps)
     e2e_t1.record(stream)
     barrier()
     host_t2 = time.time()
-    # Both loops keep the GPU busy; nvidia-smi samples about every 100 ms, so the
-    # window spans the device-timed loop and the end-to-end loop after it.
-    clk = clocks.stop(window=(host_t0, host_t2))
+    # The samples taken while either loop kept the GPU busy (not the pause between).
+    clk = clocks.stop(windows=[(host_t0, host_t1), (host_e0, host_t2)])
     e2e_ms_total = e2e_t0.elapsed_time(e2e_t1)
 
     tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)], dtype=torch.float64, device=dev)

@@ -11,7 +11,8 @@ underneath:
   (or the GEMV kernel for a single query) and a merge kernel; queries in
   pinned host memory are copied on a side stream, so a caller that issues the
   next search before reading back the previous results overlaps each upload
-  with the previous search;
+  with the previous search (a fixed ring of device buffers, nothing allocated
+  per call);
 * there is no CPU storage and no fallback: a non-CUDA device or a GPU other than
   sm_100 raises RuntimeError. ``method="torch"`` (cuBLAS + topk) remains available
   on request, as in the reference.
@@ -20,6 +21,7 @@ underneath:
 from __future__ import annotations
 
 import json
+import threading
 from pathlib import Path
 
 import numpy as np
@@ -36,37 +38,66 @@ METHODS = ("auto", "fused", "twopass", "torch")
 
 _KERNEL_DTYPES = (torch.float32, torch.float16, torch.bfloat16, torch.float64)
 
-_COPY_STREAMS: dict = {}  # device index -> side stream for host-to-device copies
 _SIDE_UPLOAD_BYTES = 256 << 10  # smaller pinned uploads stay on the current stream
+_RING_MAX_BYTES = 32 << 20  # larger pinned blocks (bulk corpus ingest) use the allocator
+_RING_SLOTS = 4
 
 
-def _copy_stream(device: torch.device) -> torch.cuda.Stream:
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    st = _COPY_STREAMS.get(idx)
-    if st is None:
-        st = _COPY_STREAMS[idx] = torch.cuda.Stream(device=idx)
-    return st
+class _UploadRing:
+    """Fixed device buffers for pinned host uploads, refilled round-robin.
 
-
-def _upload_pinned(blk: torch.Tensor, device: torch.device) -> torch.Tensor:
-    """Device copy of a pinned host block, made on a side stream.
-
-    The current stream waits for the copy (an event, no host synchronisation), so
-    the copy can run while the current stream's earlier kernels (the previous
-    search) still execute. The caller must not modify the pinned block until the
-    search is complete -- the same rule as for any non-blocking copy.
+    Each upload is copied on a side stream into the next slot; the current stream
+    waits for the copy (an event, no host synchronisation), so the copy runs while
+    the current stream's earlier kernels (the previous search) still execute. A
+    slot is refilled only after the ingest kernel that read its previous contents
+    has run (the side stream waits on an event recorded after that kernel). No
+    memory is allocated per call: growing the caching allocator's pool for a side
+    stream took cudaMalloc calls that stalled the host for milliseconds.
     """
-    cur = torch.cuda.current_stream(device)
-    side = _copy_stream(device)
-    with torch.cuda.stream(side):
-        # Allocated on the side stream, so its memory is free of the side
-        # stream's earlier work; record_stream keeps it alive for the current
-        # stream's use.
-        dst = torch.empty(blk.shape, dtype=blk.dtype, device=device)
-        dst.copy_(blk, non_blocking=True)
-    cur.wait_stream(side)
-    dst.record_stream(cur)
-    return dst
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.side = torch.cuda.Stream(device=device)
+        self.bufs: list = [None] * _RING_SLOTS
+        self.consumed = [torch.cuda.Event() for _ in range(_RING_SLOTS)]
+        self.used = [False] * _RING_SLOTS
+        self.next = 0
+        self.lock = threading.Lock()
+
+    def ingest(self, blk: torch.Tensor, out: torch.Tensor, cosine: bool, mod) -> None:
+        """Upload pinned ``blk`` and run the ingest kernel from it into ``out``."""
+        cur = torch.cuda.current_stream(self.device)
+        nelem = blk.numel()
+        with self.lock:
+            j = self.next
+            self.next = (j + 1) % _RING_SLOTS
+            if self.used[j]:
+                self.side.wait_event(self.consumed[j])
+            buf = self.bufs[j]
+            if buf is None or buf.dtype != blk.dtype or buf.numel() < nelem:
+                if buf is not None:
+                    # Queued work on the current stream may still read it.
+                    buf.record_stream(cur)
+                with torch.cuda.stream(self.side):
+                    buf = self.bufs[j] = torch.empty(nelem, dtype=blk.dtype, device=self.device)
+            dst = buf[:nelem].view(blk.shape)
+            with torch.cuda.stream(self.side):
+                dst.copy_(blk, non_blocking=True)
+            cur.wait_stream(self.side)
+            mod.ingest_into(dst, out, cosine)
+            self.consumed[j].record(cur)
+            self.used[j] = True
+
+
+_RINGS: dict = {}  # device index -> _UploadRing
+
+
+def _upload_ring(device: torch.device) -> _UploadRing:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ring = _RINGS.get(idx)
+    if ring is None:
+        ring = _RINGS[idx] = _UploadRing(torch.device("cuda", idx))
+    return ring
 
 
 def _to_tensor(a) -> torch.Tensor:
@@ -99,20 +130,21 @@ def _ingest(src: torch.Tensor, device: torch.device, cosine: bool, out: torch.Te
         mod.ingest_into(src, out, cosine)
         return out
     # Host source: stage fixed-size row blocks so a huge array never needs a
-    # second full-size copy on either side. Pinned blocks of at least
-    # _SIDE_UPLOAD_BYTES go through the side stream (the extra host work of the
-    # stream switch outweighs the overlap for small ones).
+    # second full-size copy on either side. Contiguous pinned blocks of at least
+    # _SIDE_UPLOAD_BYTES go through the upload ring's side stream (the extra host
+    # work of the stream switch outweighs the overlap for small ones).
     pinned = src.is_pinned()
     with torch.cuda.device(device):
         for start in range(0, n, _INGEST_CHUNK):
             blk = src if n <= _INGEST_CHUNK else src[start : start + _INGEST_CHUNK]
-            if pinned and blk.nbytes >= _SIDE_UPLOAD_BYTES and blk.is_contiguous():
-                blk_dev = _upload_pinned(blk, device)
-            else:
-                blk_dev = blk.to(device, non_blocking=pinned)
+            dst = out if n <= _INGEST_CHUNK else out[start : start + blk.shape[0]]
+            if pinned and _SIDE_UPLOAD_BYTES <= blk.nbytes <= _RING_MAX_BYTES and blk.is_contiguous():
+                _upload_ring(device).ingest(blk, dst, cosine, mod)
+                continue
+            blk_dev = blk.to(device, non_blocking=pinned)
             if blk_dev.stride(1) != 1:
                 blk_dev = blk_dev.contiguous()
-            mod.ingest_into(blk_dev, out if n <= _INGEST_CHUNK else out[start : start + blk.shape[0]], cosine)
+            mod.ingest_into(blk_dev, dst, cosine)
     return out
 
 

@@ -163,19 +163,29 @@ def test_plan_selects_gemv_only_for_one_query(cvs, b, expect_gemv):
 
 
 def test_pinned_host_queries_back_to_back(cvs):
-    """Pinned host queries are uploaded on a side stream; several searches issued
-    back to back (no host synchronisation between them) must each see their own
-    queries and match the device-query results."""
-    x, q = _data(20000, 256, 300, seed=5)
+    """Pinned host query blocks of 256 KB and more go through a ring of four
+    device upload slots on a side stream. Ten searches issued back to back behind
+    a busy stream (no host synchronisation between them) must each see their own
+    queries: a slot is refilled only after the ingest that read it has run, and a
+    slot that grows, or changes dtype, keeps its old buffer alive for queued work."""
+    import cuda_vector_search.index as ix
+
+    x, q = _data(20000, 256, 3600, seed=5)
     index = cvs.Index(x.cuda(), metric="cosine")
-    parts = [q[i * 100:(i + 1) * 100] for i in range(3)]
+    sizes = [260, 300, 280, 320, 400, 260, 300, 500, 270, 290]  # rows of 256 fp32 >= 256 KB
+    starts = [sum(sizes[:j]) for j in range(len(sizes))]
+    parts = [q[s0:s0 + n].float() for s0, n in zip(starts, sizes)]
+    parts[6] = parts[6].double()  # a slot switching dtype
     ref = [index.search(p.cuda(), 10) for p in parts]
-    pinned = [p.float().pin_memory() for p in parts]
+    pinned = [p.pin_memory() for p in parts]
+    assert all(p.nbytes >= ix._SIDE_UPLOAD_BYTES for p in pinned)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(20_000_000)  # the host runs ahead of the GPU
     outs = [index.search(p, 10) for p in pinned]
     torch.cuda.synchronize()
     for (rv, ri), (v, i) in zip(ref, outs):
         assert torch.equal(ri, i)
-        assert torch.allclose(rv, v, atol=0, rtol=0)
+        assert torch.equal(rv, v)
 
 
 @pytest.mark.parametrize("b,tile", [(200, 256), (256, 256), (300, 128), (384, 128), (512, 256), (640, 128)])
