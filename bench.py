@@ -312,26 +312,39 @@ def run_ours(args, cfg):
     # It starts from the same rested state as the loop above: after ~200 ms of
     # back-to-back searches the 1 kW power cap lowers the SM clock, and without
     # the pause this loop would run in that window while the first did not.
-    # Each step's results land in pinned host buffers (stream-ordered copies); the
-    # barrier after the loop waits for the last of them. Step s's results are
-    # read back after step s+1 has been issued (a two-deep pipeline, as a serving
-    # loop would run it), so step s+1's query upload is not queued behind them.
-    # The pinned result buffers are allocated, and the path warmed up (side copy
-    # stream, allocator blocks), before the timed loop: a pinned allocation
+    # Each step's results land in pinned host buffers; the barrier after the loop
+    # waits for the last of them. As a serving loop would run it, step s's results
+    # are read back on a read-back stream after step s+1 has been issued, so the
+    # copy overlaps step s+1's search and step s+1's query upload is not queued
+    # behind it. The compute stream waits for that copy before step s+2, so the
+    # result tensors' memory is reused in stream order (no record_stream, which
+    # would make the allocator grow its pool with cudaMalloc calls that stall the
+    # host). The pinned result buffers are allocated, and the path warmed up
+    # (upload ring, allocator blocks), before the timed loop: a pinned allocation
     # (cudaHostAlloc) takes milliseconds and leaves the GPU idle meanwhile.
     v_host = torch.empty((b, k), dtype=torch.float32, pin_memory=True)
     i_host = torch.empty((b, k), dtype=torch.int64, pin_memory=True)
+    rb_stream = torch.cuda.Stream(device=dev)
+    searched = [torch.cuda.Event() for _ in range(2)]
+    read_back = torch.cuda.Event()
+
+    def read(res, ev):
+        rb_stream.wait_event(ev)
+        with torch.cuda.stream(rb_stream):
+            v_host.copy_(res[0], non_blocking=True)
+            i_host.copy_(res[1], non_blocking=True)
+        read_back.record(rb_stream)
+        stream.wait_event(read_back)
 
     def e2e_loop(steps):
         prev = None
-        for _ in range(steps):
+        for s in range(steps):
             cur = index.search(q_host, k)
+            searched[s & 1].record(stream)
             if prev is not None:
-                v_host.copy_(prev[0], non_blocking=True)
-                i_host.copy_(prev[1], non_blocking=True)
+                read(prev, searched[(s - 1) & 1])
             prev = cur
-        v_host.copy_(prev[0], non_blocking=True)
-        i_host.copy_(prev[1], non_blocking=True)
+        read(prev, searched[(steps - 1) & 1])
 
     e2e_loop(max(args.warmup, 3))
     e2e_t0, e2e_t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
