@@ -24,6 +24,16 @@ namespace {
 constexpr int kIngestThreads = 256;
 constexpr int kIngestMaxPerLane = 64;  // d <= 2048 handled from registers
 
+// The ingest kernels are launched programmatically (launch_programmatic): they
+// may be scheduled while the previous kernel on the stream finishes, and wait
+// for it (its writes to the source, its reads of memory the destination may
+// reuse) before touching memory. The next kernel may likewise be scheduled
+// early; it waits for this grid in the same way.
+__device__ __forceinline__ void ingest_prologue() {
+  grid_launch_dependents();
+  grid_dependency_wait();
+}
+
 template <int T>
 __device__ __forceinline__ __half load_as_half(const void* src, size_t i) {
   if constexpr (T == kSrcF32) return __float2half_rn(static_cast<const float*>(src)[i]);
@@ -37,6 +47,7 @@ template <int T>
 __global__ void __launch_bounds__(kIngestThreads) ingest_kernel(const void* src, long long n, int d,
                                                                 long long src_stride, int d_pad,
                                                                 int cosine, __half* dst) {
+  ingest_prologue();
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (kIngestThreads / 32);
   for (long long row = static_cast<long long>(blockIdx.x) * (kIngestThreads / 32) + (threadIdx.x >> 5);
@@ -106,6 +117,7 @@ template <int T, int CPL>
 __global__ void __launch_bounds__(kIngestThreads) ingest_vec_kernel(const void* src, long long n, int d,
                                                                     long long src_stride, int d_pad,
                                                                     int cosine, __half* dst) {
+  ingest_prologue();
   const int lane = threadIdx.x & 31;
   const int dchunks = d >> 3, pchunks = d_pad >> 3;
   const long long warps = static_cast<long long>(gridDim.x) * (kIngestThreads / 32);
@@ -156,8 +168,8 @@ cudaError_t launch_vec(const void* src, long long n, int d, long long src_stride
   const int cpl = (d_pad / 8 + 31) / 32;
 #define CVS_INGEST_VEC(C)                                                                          \
   if (cpl <= C) {                                                                                 \
-    ingest_vec_kernel<T, C><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); \
-    return cudaGetLastError();                                                                     \
+    return launch_programmatic(ingest_vec_kernel<T, C>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, \
+                               src_stride, d_pad, cosine, dst);                                    \
   }
   CVS_INGEST_VEC(1) CVS_INGEST_VEC(2) CVS_INGEST_VEC(3) CVS_INGEST_VEC(4) CVS_INGEST_VEC(6) CVS_INGEST_VEC(8)
 #undef CVS_INGEST_VEC
@@ -186,14 +198,27 @@ cudaError_t ingest_launch(const void* src, int src_dtype, long long n, int d, lo
       default: return cudaErrorInvalidValue;
     }
   }
+  cudaError_t e;
   switch (src_dtype) {
-    case kSrcF32: ingest_kernel<kSrcF32><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); break;
-    case kSrcF16: ingest_kernel<kSrcF16><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); break;
-    case kSrcBF16: ingest_kernel<kSrcBF16><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); break;
-    case kSrcF64: ingest_kernel<kSrcF64><<<grid, kIngestThreads, 0, stream>>>(src, n, d, src_stride, d_pad, cosine, dst); break;
+    case kSrcF32:
+      e = launch_programmatic(ingest_kernel<kSrcF32>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
+                              d_pad, cosine, dst);
+      break;
+    case kSrcF16:
+      e = launch_programmatic(ingest_kernel<kSrcF16>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
+                              d_pad, cosine, dst);
+      break;
+    case kSrcBF16:
+      e = launch_programmatic(ingest_kernel<kSrcBF16>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
+                              d_pad, cosine, dst);
+      break;
+    case kSrcF64:
+      e = launch_programmatic(ingest_kernel<kSrcF64>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
+                              d_pad, cosine, dst);
+      break;
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+  return e;
 }
 
 }  // namespace cvs

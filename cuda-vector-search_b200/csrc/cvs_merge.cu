@@ -141,7 +141,9 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
   int* s_warp = reinterpret_cast<int*>(s_bound + 2);  // [kKeysWarps]
   int* s_off = s_warp + kKeysWarps;                   // [kScanLists]
   // Launched as a programmatic dependent of the search kernel: everything the
-  // search kernel wrote is visible once this returns.
+  // search kernel wrote is visible once this returns. (It does not release the
+  // next kernel early: measured, letting the next call's ingest and workspace
+  // clear become resident during the merge gained nothing.)
   grid_dependency_wait();
   const uint64_t* base = a.part + static_cast<size_t>(q) * a.lists * a.stride;
   const int* counts = a.counts ? a.counts + static_cast<size_t>(q) * a.lists : nullptr;
@@ -342,6 +344,9 @@ size_t merge_smem(int k) { return kMergeWarps * merge_warp_bytes(k); }
 __global__ void __launch_bounds__(256) prepare_kernel(uint32_t* p, size_t words, const uint4* q_src, uint4* q_dst,
                                                       size_t q_chunks, size_t pad_chunks) {
   grid_launch_dependents();
+  // Launched programmatically: the previous kernel (the query ingest, or the
+  // previous call's merge, which reads the workspace) finishes first.
+  grid_dependency_wait();
   const size_t stride = static_cast<size_t>(gridDim.x) * 256;
   for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < words; i += stride) p[i] = 0u;
   for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < pad_chunks; i += stride)
@@ -373,9 +378,8 @@ cudaError_t prepare_launch(void* p, size_t bytes, const void* q_src, void* q_dst
   const size_t work = std::max(words, pad_chunks);
   if (work == 0) return cudaSuccess;
   const unsigned grid = static_cast<unsigned>(std::min<size_t>((work + 255) / 256, 1024));
-  prepare_kernel<<<grid, 256, 0, stream>>>(static_cast<uint32_t*>(p), words, static_cast<const uint4*>(q_src),
-                                           static_cast<uint4*>(q_dst), q_chunks, pad_chunks);
-  return cudaGetLastError();
+  return launch_programmatic(prepare_kernel, dim3(grid), dim3(256), 0, stream, static_cast<uint32_t*>(p), words,
+                             static_cast<const uint4*>(q_src), static_cast<uint4*>(q_dst), q_chunks, pad_chunks);
 }
 
 cudaError_t merge_lists_launch(const MergeListsArgs& a, cudaStream_t stream) {
