@@ -40,6 +40,8 @@ for _p in (ROOT, ROOT / "cuda-vector-search_b200"):
 METRIC = "QPS and % roofline (TC TFLOP/s or HBM GB/s), 1M×768 b256 k10, 1–8 B200"
 CHUNK = 1 << 18
 
+L2_BYTES = 126 << 20  # B200 L2 size, rounded up
+
 CONFIGS = {
     # name: rows per GPU, dim, batch, k, metric
     "c1": dict(n=100_000, d=384, b=32, k=10, metric="cosine"),
@@ -285,6 +287,17 @@ def run_ours(args, cfg):
         step(q_dev)
     barrier()
 
+    # A corpus that fits in L2 would stay there from one step to the next; such
+    # configs write a buffer twice the L2 size before every timed step, outside
+    # the step's CUDA-event interval, and time the steps one by one.
+    corpus_bytes = 2 * n * local_index._x.shape[1]
+    flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if corpus_bytes < 2 * L2_BYTES else None
+    step_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(args.steps)] if flush_buf is not None else []
+
+    def flush(s):
+        flush_buf.fill_(s & 255)
+
     # Timed region: device-resident queries, CUDA events on the launching stream.
     stream = torch.cuda.current_stream()
     ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -299,13 +312,18 @@ def run_ours(args, cfg):
     host_t0 = time.time()
     t0.record(stream)
     for s in range(args.steps):
+        if flush_buf is not None:
+            flush(s)
+            step_evs[s][0].record(stream)
         mod.set_profile_events(ev_pairs[s][0].cuda_event, ev_pairs[s][1].cuda_event)
         step(q_dev)
+        if flush_buf is not None:
+            step_evs[s][1].record(stream)
     t1.record(stream)
     barrier()
     host_t1 = time.time()
     mod.set_profile_events(0, 0)
-    ms_total = t0.elapsed_time(t1)
+    ms_total = sum(a.elapsed_time(bb) for a, bb in step_evs) if flush_buf is not None else t0.elapsed_time(t1)
     kern_ms = [a.elapsed_time(bb) for a, bb in ev_pairs]
 
     # End to end through the public API: pinned host fp32 queries in, host results out.
@@ -336,6 +354,18 @@ def run_ours(args, cfg):
         read_back.record(rb_stream)
         stream.wait_event(read_back)
 
+    def e2e_loop_flushed(steps):
+        # One step at a time (no pipelining across the flushes), each timed alone.
+        for s in range(steps):
+            flush(s)
+            step_evs[s][0].record(stream)
+            cur = index.search(q_host, k)
+            v_host.copy_(cur[0], non_blocking=True)
+            i_host.copy_(cur[1], non_blocking=True)
+            step_evs[s][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(bb) for a, bb in step_evs[:steps])
+
     def e2e_loop(steps):
         prev = None
         for s in range(steps):
@@ -352,13 +382,15 @@ def run_ours(args, cfg):
     barrier()
     host_e0 = time.time()
     e2e_t0.record(stream)
-    e2e_loop(args.steps)
+    e2e_flushed_ms = e2e_loop_flushed(args.steps) if flush_buf is not None else None
+    if flush_buf is None:
+        e2e_loop(args.steps)
     e2e_t1.record(stream)
     barrier()
     host_t2 = time.time()
     # The samples taken while either loop kept the GPU busy (not the pause between).
     clk = clocks.stop(windows=[(host_t0, host_t1), (host_e0, host_t2)])
-    e2e_ms_total = e2e_t0.elapsed_time(e2e_t1)
+    e2e_ms_total = e2e_flushed_ms if flush_buf is not None else e2e_t0.elapsed_time(e2e_t1)
 
     tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -406,7 +438,10 @@ def run_ours(args, cfg):
                 "config": args.config,
                 "rows_per_gpu": n, "total_rows": n * world, "dim": d, "batch": b, "k": k,
                 "metric": cfg["metric"],
-                "l2": f"inputs larger than L2 ({2 * n * d_pad / 1e9:.2f} GB corpus per GPU vs 126 MB L2)",
+                "l2": (f"corpus ({corpus_bytes / 1e9:.3f} GB per GPU) fits in the 126 MB L2: a {2 * L2_BYTES >> 20} MiB "
+                       "buffer is written before every timed step, outside the step's CUDA-event interval; "
+                       "the end-to-end steps then run one at a time") if flush_buf is not None else
+                      f"inputs larger than L2 ({corpus_bytes / 1e9:.2f} GB corpus per GPU vs 126 MB L2)",
                 "value_unit": "queries x 1M-row shards per second over all ranks (N*b/t)" if world > 1
                               else "queries per second",
                 "qps_global": round(b / (ms / 1e3), 1),
