@@ -534,7 +534,10 @@ def run_sweep(args, cfg):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    # 200 steps: ~80 ms at C2, long enough for several clock samples inside the
+    # timed loop (nvidia-smi samples every 20 ms), short enough to stay below
+    # the power cap's reaction time.
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
