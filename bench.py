@@ -131,6 +131,13 @@ def run_reference(args, cfg):
     W = max(args.warmup, 0)
     rows = min(cfg["n"], 65536)
     x16, q16 = cpu_sample(cfg, rows, seed=7)
+    # Each step is a bounded sample: if K steps of 65536 rows would take more
+    # than ~90 s on this host, fewer rows per step (at least 8192).
+    t1 = time_cpu_step(cfg, x16, q16)
+    budget = 90.0 / max(args.steps, 1)
+    if t1 > budget and rows > 8192:
+        rows = max(8192, int(rows * budget / t1) // 1024 * 1024)
+        x16, q16 = cpu_sample(cfg, rows, seed=7)
     for _ in range(min(W, 2)):
         time_cpu_step(cfg, x16, q16)
     times = [time_cpu_step(cfg, x16, q16) for _ in range(args.steps)]
