@@ -1,4 +1,4 @@
-"""Benchmark: exact top-k search QPS on B200, with roofline and CPU baseline.
+"""Benchmark: exact top-k search QPS on B200, with roofline, parity and CPU baseline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
 
@@ -6,13 +6,17 @@ One step = one search of a query batch against the corpus, with queries and
 corpus already resident in HBM (`value`); `e2e` repeats it through the public
 API from pinned host queries (fp32) to host results. Default workload (config
 c2): 1M x 768 fp16 unit-norm corpus PER GPU, batch 256, k=10, cosine. With N>1
-ranks (torchrun) the corpus is row-sharded: rank r holds its own 1M rows, each
-step is a full sharded search (local fused top-k + NCCL all-gather + merge), and
-`value` counts query x 1M-row-shard units per second over all ranks (N*b/t).
+ranks (torchrun) the corpus is row-sharded: rank r holds its own rows (global
+chunks r*shard .. of the same generator), each step is a full sharded search
+(local fused top-k + NCCL all-gather + merge), and `value` counts query x
+shard units per second over all ranks (N*b/t); `qps_global` is b/t over the
+whole N-shard corpus and `phases_us` splits a step into local search,
+all-gather and merge. After the timed loops, `parity` checks a subset of query
+rows of the search result against the CPU oracle on the stored corpus.
 
---impl reference times the reference's CPU path restated in numpy (oracle/,
-fp32 matmul + top-k with the reference's chunked merge) on the host cores, on a
-bounded sample of the same workload, scaled to the same unit.
+--impl reference times the reference's CPU search paths (oracle/cpu_paths.py:
+Index(device="cpu") torch fp32, exact_topk_fp32, numpy_search) on the host
+cores, on a bounded sample of the same workload, scaled to the same unit.
 
 --sweep [--sweep-batches 1,8,256 --sweep-chunks 0,74 --report table.md] times the
 search over batch sizes and plan hints on one GPU instead (JSON rows + a
@@ -76,9 +80,45 @@ def workload_name(cfg) -> str:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the reference's fp32 CPU path restated in numpy (oracle/)
+# Shared by both arms
 # ---------------------------------------------------------------------------
+def bench_config(args, cfg, world: int) -> dict:
+    """The `config` object of the JSON line; identical in both arms."""
+    d_pad = -(-cfg["d"] // 64) * 64
+    corpus_bytes = 2 * cfg["n"] * d_pad
+    flushed = corpus_bytes < 2 * L2_BYTES
+    return {
+        "workload": workload_name(cfg),
+        "config": args.config,
+        "rows_per_gpu": cfg["n"], "total_rows": cfg["n"] * world, "dim": cfg["d"], "batch": cfg["b"],
+        "k": cfg["k"], "metric": cfg["metric"],
+        "l2": (f"corpus ({corpus_bytes / 1e9:.3f} GB per GPU) fits in the 126 MB L2: a {2 * L2_BYTES >> 20} MiB "
+               "buffer is written before every timed step, outside the step's CUDA-event interval; "
+               "the end-to-end steps then run one at a time") if flushed else
+              f"inputs larger than L2 ({corpus_bytes / 1e9:.2f} GB corpus per GPU vs 126 MB L2)",
+        "value_unit": (f"queries x {cfg['n'] // 1000}k-row shards per second over all ranks (N*b/t)" if world > 1
+                       else "queries per second"),
+    }
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's CPU search paths (oracle/cpu_paths.py)
+# ---------------------------------------------------------------------------
+CPU_SAMPLE_ROWS = 1 << 18  # one chunk of the reference's exact_topk_fp32
+
+
 def cpu_sample(cfg, rows: int, seed: int):
+    """Unit-norm fp16 corpus rows and queries with the benchmark's distribution."""
     import numpy as np
 
     rng = np.random.default_rng(seed)
@@ -89,68 +129,102 @@ def cpu_sample(cfg, rows: int, seed: int):
     return x.astype(np.float16), q.astype(np.float16)
 
 
-def time_cpu_step(cfg, x16, q16):
-    """One bounded step of the CPU path; returns seconds."""
+def cpu_paths(cfg, rows: int):
+    """{name: (callable running one search of all queries over the sample, what it is)}.
+
+    Each callable includes the per-call query preparation of its path (cosine
+    normalisation), as the reference's search does."""
     import numpy as np
+    import torch
 
-    from oracle import exact_topk, normalize_rows_fp16
+    from oracle import index_cpu_search, normalize_rows_fp16, numpy_search, torch_exact_topk_fp32
 
-    t0 = time.perf_counter()
-    q = normalize_rows_fp16(q16) if cfg["metric"] == "cosine" else q16
-    exact_topk(q.astype(np.float32), x16, cfg["k"])
-    return time.perf_counter() - t0
-
-
-def cpu_baseline(cfg, budget_s: float = 12.0):
-    import numpy as np  # noqa: F401
-
-    rows = min(cfg["n"], 131072)
+    torch.set_num_threads(os.cpu_count() or 1)
     x16, q16 = cpu_sample(cfg, rows, seed=7)
-    time_cpu_step(cfg, x16[:4096], q16)  # warm the BLAS threads
-    times = []
-    t_start = time.perf_counter()
-    while len(times) < 3 or (time.perf_counter() - t_start < budget_s and len(times) < 20):
-        times.append(time_cpu_step(cfg, x16, q16))
-    t = statistics.median(times)
-    qps = cfg["b"] / (t * cfg["n"] / rows)
+    cos = cfg["metric"] == "cosine"
+    k = cfg["k"]
+    x32_t = torch.from_numpy(x16.astype(np.float32))  # Index(device="cpu") stores fp32 rows
+    x16_t = torch.from_numpy(x16)
+    x32_np = x16.astype(np.float32)
+    q_t = torch.from_numpy(q16).float()
+
+    def prep_t():
+        return q_t / q_t.norm(dim=1, keepdim=True).clamp_min(1e-12) if cos else q_t
+
+    def prep_np():
+        return normalize_rows_fp16(q16).astype(np.float32) if cos else q16.astype(np.float32)
+
     return {
-        "value": round(qps, 2),
+        "torch_index_cpu": (lambda: index_cpu_search(prep_t(), x32_t, k),
+                            "reference Index(device='cpu').search: fp32 torch.matmul + torch.topk "
+                            "(index.py:131, reference.py:8-15)"),
+        "torch_exact_topk_fp32": (lambda: torch_exact_topk_fp32(prep_t(), x16_t, k),
+                                  "reference exact_topk_fp32 on the fp16 rows (reference.py:18-34)"),
+        "numpy_search": (lambda: numpy_search(prep_np(), x32_np, k),
+                         "reference numpy_search (bench/bench_baselines.py:45-50)"),
+    }
+
+
+def cpu_baseline(cfg):
+    """The three reference CPU paths timed with the reference's median method
+    (bench/timing.py) on a 2^18-row sample; the fastest is the baseline."""
+    rows = min(cfg["n"], CPU_SAMPLE_ROWS)
+    scale = cfg["n"] / rows
+    from oracle import time_call
+
+    paths = {}
+    for name, (fn, what) in cpu_paths(cfg, rows).items():
+        ms, reps = time_call(fn, target_s=1.0, max_reps=20)
+        paths[name] = {"ms_per_sample": round(ms, 3), "reps": reps,
+                       "qps": round(cfg["b"] / (ms / 1e3 * scale), 2), "what": what}
+    best = min(paths, key=lambda nm: paths[nm]["ms_per_sample"])
+    return {
+        "value": paths[best]["qps"],
         "unit": "QPS",
         "cores": os.cpu_count(),
+        "cpu_model": cpu_model(),
         "kind": "port",
-        "sample": (f"all {cfg['b']} queries x {rows} of {cfg['n']} corpus rows per step "
-                   f"(median of {len(times)}), scaled linearly to {cfg['n']} rows; numpy fp32 matmul + "
-                   f"top-k with the reference's chunked merge (oracle/exact.py)"),
+        "path": best,
+        "sample": (f"all {cfg['b']} queries x {rows} of {cfg['n']} corpus rows per call (median of reps, "
+                   f"reference bench/timing.py method), scaled x{scale:.3g} to the full corpus; fastest of "
+                   f"the reference's three CPU paths, restated in oracle/cpu_paths.py"),
+        "paths": paths,
     }
 
 
 def run_reference(args, cfg):
+    """The reference's CPU implementation of the search on the host cores.
+
+    Each step is one call of the fastest of the reference's CPU paths (chosen by
+    a short median timing first) over a bounded sample: all queries against up
+    to 2^18 corpus rows, fewer if K steps would take more than ~90 s. The line's
+    ms_per_step is the measured time of such a step; `value` scales it to the
+    full corpus (config rows / sample rows, given as `row_scale`)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    from oracle import time_call
+
     W = max(args.warmup, 0)
-    rows = min(cfg["n"], 65536)
-    x16, q16 = cpu_sample(cfg, rows, seed=7)
-    # Each step is a bounded sample: if K steps of 65536 rows would take more
-    # than ~90 s on this host, fewer rows per step (at least 8192).
-    t1 = time_cpu_step(cfg, x16, q16)
-    budget = 90.0 / max(args.steps, 1)
-    if t1 > budget and rows > 8192:
-        rows = max(8192, int(rows * budget / t1) // 1024 * 1024)
-        x16, q16 = cpu_sample(cfg, rows, seed=7)
-    for _ in range(min(W, 2)):
-        time_cpu_step(cfg, x16, q16)
-    times = [time_cpu_step(cfg, x16, q16) for _ in range(args.steps)]
-    t = sum(times) / len(times) * cfg["n"] / rows
-    qps = cfg["b"] / t
-    base = {
-        "value": round(qps, 2),
-        "unit": "QPS",
-        "cores": os.cpu_count(),
-        "kind": "port",
-        "sample": (f"each step: all {cfg['b']} queries x {rows} of {cfg['n']} corpus rows, scaled "
-                   f"linearly to {cfg['n']} rows; numpy restatement of the reference CPU path (oracle/)"),
-    }
+    rows = min(cfg["n"], CPU_SAMPLE_ROWS)
+    paths = cpu_paths(cfg, rows)
+    probe = {nm: time_call(fn, target_s=0.3, max_reps=5)[0] for nm, (fn, _) in paths.items()}
+    best = min(probe, key=probe.get)
+    budget_ms = 90e3 / max(args.steps, 1)
+    if probe[best] > budget_ms and rows > 8192:
+        rows = max(8192, int(rows * budget_ms / probe[best]) // 1024 * 1024)
+        paths = cpu_paths(cfg, rows)
+    fn, what = paths[best]
+    for _ in range(min(W, 3)):
+        fn()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    t = sum(times) / len(times)
+    scale = cfg["n"] / rows
+    qps = cfg["b"] / (t * scale)
     out = {
         "impl": "reference",
         "metric": METRIC,
@@ -160,13 +234,22 @@ def run_reference(args, cfg):
         "steps": args.steps,
         "warmup": W,
         "ms_per_step": round(t * 1e3, 3),
+        "ms_per_step_median": round(statistics.median(times) * 1e3, 3),
+        "row_scale": round(scale, 4),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": workload_name(cfg), **cfg},
-        "cpu_baseline": base,
+        "config": bench_config(args, cfg, args.gpus),
+        "cpu_baseline": {
+            "value": round(qps, 2), "unit": "QPS", "cores": os.cpu_count(), "cpu_model": cpu_model(),
+            "kind": "port", "path": best,
+            "sample": (f"each step: all {cfg['b']} queries x {rows} of {cfg['n']} corpus rows through {what}; "
+                       f"ms_per_step is that measured step, value scales it x{scale:.4g} to the full corpus; "
+                       f"path chosen as the fastest of {sorted(probe)} by a median timing "
+                       f"({', '.join(f'{k}={v:.1f} ms' for k, v in sorted(probe.items()))})"),
+        },
         "e2e": {"value": round(qps, 2), "unit": "QPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
@@ -247,6 +330,55 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(inside), "power_w_median": statistics.median(pw) if pw else None,
                 "window": "timed region" if inside is not rows else "whole run (too few samples inside)"}
+
+
+def parity_check(torch, local_index, q_dev, result, k, row_offset, world, rows=8):
+    """Checks `rows` query rows of a finished search against the CPU oracle.
+
+    Every rank streams its own stored shard to the host in 2^19-row blocks and
+    computes the oracle's top-(k+1) for the selected queries with global row
+    ids; rank 0 merges the ranks' lists (oracle.merge_topk) and compares them
+    with the search result. Runs after the timed loops, never inside them.
+    Returns the comparison on rank 0 (None elsewhere)."""
+    import numpy as np
+    import torch.distributed as dist
+
+    from oracle import compare_topk, exact_topk_blocks, merge_topk
+
+    d = local_index.dim
+    b = q_dev.shape[0]
+    sel = np.unique(np.linspace(0, b - 1, min(b, rows)).astype(np.int64))
+    dev = q_dev.device
+    q32 = local_index._prep_queries(q_dev)[torch.as_tensor(sel, device=dev), :d].float().cpu().numpy()
+    x = local_index._x
+
+    def blocks(step=1 << 19):
+        for s in range(0, x.shape[0], step):
+            yield row_offset + s, x[s : s + step].cpu()[:, :d].float().numpy()
+
+    kk = k + 1
+    lv, li = exact_topk_blocks(q32, blocks(), kk)
+    if lv.shape[1] < kk:  # a shard with fewer rows than k + 1
+        pad = kk - lv.shape[1]
+        lv = np.concatenate([lv, np.full((lv.shape[0], pad), -np.inf, np.float32)], 1)
+        li = np.concatenate([li, np.full((li.shape[0], pad), np.iinfo(np.int64).max, np.int64)], 1)
+    if world > 1:
+        tv = torch.from_numpy(np.ascontiguousarray(lv)).to(dev)
+        ti = torch.from_numpy(np.ascontiguousarray(li)).to(dev)
+        gv = torch.empty((world,) + tuple(tv.shape), dtype=tv.dtype, device=dev)
+        gi = torch.empty((world,) + tuple(ti.shape), dtype=ti.dtype, device=dev)
+        dist.all_gather_into_tensor(gv, tv)
+        dist.all_gather_into_tensor(gi, ti)
+        gv, gi = gv.cpu().numpy(), gi.cpu().numpy()
+        lv, li = merge_topk(list(gv), list(gi), kk)
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    got_v = result[0].cpu().numpy()[sel]
+    got_i = result[1].cpu().numpy()[sel]
+    res = compare_topk(got_v, got_i, lv, li, k)
+    res["what"] = (f"{len(sel)} of {b} query rows (evenly spaced) of one search after the timed loops, vs the CPU "
+                   f"oracle (numpy fp32 exact top-k, oracle/exact.py) on the stored corpus of all {world} rank(s)")
+    return res
 
 
 def run_ours(args, cfg):
@@ -399,10 +531,26 @@ def run_ours(args, cfg):
     clk = clocks.stop(windows=[(host_t0, host_t1), (host_e0, host_t2)])
     e2e_ms_total = e2e_flushed_ms if flush_buf is not None else e2e_t0.elapsed_time(e2e_t1)
 
-    tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)], dtype=torch.float64, device=dev)
+    # Untimed afterwards: where a sharded step's time goes (CUDA events on the
+    # current stream around the local search, the all-gather and the merge).
+    phases = [0.0, 0.0, 0.0]
+    if world > 1:
+        pev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        index.phase_events = pev
+        reps = min(args.steps, 20)
+        for _ in range(reps):
+            step(q_dev)
+            pev[3].synchronize()
+            for j in range(3):
+                phases[j] += pev[j].elapsed_time(pev[j + 1]) * 1e3 / reps
+        index.phase_events = None
+    tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)] + phases, dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms_total, e2e_ms_total, kern_total = tt.tolist()
+    ms_total, e2e_ms_total, kern_total = tt.tolist()[:3]
+    phases = tt.tolist()[3:]
+    parity = None if args.no_parity else parity_check(torch, local_index, q_dev, step(q_dev), k,
+                                                       index.row_offset if world > 1 else 0, world)
     ms = ms_total / args.steps
     kern_avg = kern_total / args.steps
     value = world * b / (ms / 1e3)
@@ -426,7 +574,9 @@ def run_ours(args, cfg):
                     "frac": round(gbs / hbm_peak, 4), "traffic": traffic,
                     "note": f"copy bandwidth, {peak_src}; algorithmic bytes = corpus + queries + results"}
         roofline = roof_tc if bound == "tensor" else roof_hbm
-        launches_per_step = 3 if world == 1 else 4  # ingest, search, merge (+ shard merge)
+        # Our kernels per step: query ingest, workspace prepare, search, merge of
+        # the segment lists (+ the merge of the gathered shard lists).
+        launches_per_step = 4 if world == 1 else 5
         out = {
             "metric": METRIC,
             "value": round(value, 1),
@@ -440,19 +590,8 @@ def run_ours(args, cfg):
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic",
-            "config": {
-                "workload": workload_name(cfg),
-                "config": args.config,
-                "rows_per_gpu": n, "total_rows": n * world, "dim": d, "batch": b, "k": k,
-                "metric": cfg["metric"],
-                "l2": (f"corpus ({corpus_bytes / 1e9:.3f} GB per GPU) fits in the 126 MB L2: a {2 * L2_BYTES >> 20} MiB "
-                       "buffer is written before every timed step, outside the step's CUDA-event interval; "
-                       "the end-to-end steps then run one at a time") if flush_buf is not None else
-                      f"inputs larger than L2 ({corpus_bytes / 1e9:.2f} GB corpus per GPU vs 126 MB L2)",
-                "value_unit": "queries x 1M-row shards per second over all ranks (N*b/t)" if world > 1
-                              else "queries per second",
-                "qps_global": round(b / (ms / 1e3), 1),
-            },
+            "config": bench_config(args, cfg, world),
+            "qps_global": round(b / (ms / 1e3), 1),
             "roofline": roofline,
             "roofline_other": roof_hbm if bound == "tensor" else roof_tc,
             "kernel_ms": round(kern_avg, 4),
@@ -461,7 +600,12 @@ def run_ours(args, cfg):
                     "d2h_bytes_per_step": int(v_host.numel() * 4 + i_host.numel() * 8)},
             "clocks": clk,
             "gpu_launches": launches_per_step * args.steps,
+            "parity": parity,
         }
+        if world > 1:
+            out["phases_us"] = {"local_search": round(phases[0], 1), "all_gather": round(phases[1], 1),
+                                "merge": round(phases[2], 1),
+                                "note": "max over ranks of the mean of up to 20 untimed steps after the timed loops"}
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(cfg)
         print(json.dumps(out), flush=True)
@@ -549,6 +693,7 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the post-timing oracle check (profiling runs)")
     ap.add_argument("--rows", type=int, default=0, help="override rows per GPU (profiling runs)")
     ap.add_argument("--batch", type=int, default=0, help="override the batch size (profiling runs)")
     ap.add_argument("--sweep", action="store_true", help="plan sweep instead of the benchmark line")

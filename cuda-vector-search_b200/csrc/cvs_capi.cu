@@ -26,6 +26,7 @@ namespace {
 __device__ int g_device_error;  // one word per device; written by kernels on a failed wait
 
 thread_local std::string g_last_error;
+thread_local int64_t g_stall_cycles = 0;  // armed failure-path test (cvs_debug_stall_next_search)
 
 cvs_status fail(cvs_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 cvs_status fail(cvs_status s, const char* fmt, ...) {
@@ -150,7 +151,10 @@ int pair_clusters(int epi, bool qres, int ksl, int sms) {
   static std::unordered_map<long long, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const long long key = (static_cast<long long>(dev) << 32) | (epi << 16) | (qres ? 1 << 8 : 0) | ksl;
+  // dev | epilogue | resident flag | K slices, each in its own field (ksl is
+  // d_pad / 64, unbounded by the C ABI, so it gets the low 31 bits).
+  const long long key = (static_cast<long long>(dev) << 40) | (static_cast<long long>(epi) << 32) |
+                        (qres ? 1LL << 31 : 0LL) | static_cast<long long>(ksl);
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
@@ -318,6 +322,10 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     plan_out[1] = p.segs;
   }
   if (b == 0) return CVS_OK;
+  const int64_t stall_cycles = g_stall_cycles;
+  g_stall_cycles = 0;  // one call only
+  if (stall_cycles > 0 && (p.gemv || p.pair))
+    return fail(CVS_ERR_INVALID_ARGUMENT, "the stall test hook needs a one-CTA tcgen05 plan (2..128 queries)");
   if (!out_scores || !out_ids) return fail(CVS_ERR_INVALID_ARGUMENT, "null output pointer");
   if (!workspace || workspace_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) != 0)
     return fail(CVS_ERR_WORKSPACE, "workspace of %zu bytes (256-byte aligned) required, got %zu at %p",
@@ -383,6 +391,10 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
     // dry tile gives the other CTAs' bound refresh a tile's time to land.
     a.dry = p.tiles_per_seg >= 3 ? kDryTiles : (p.tiles_per_seg == 2 ? 1 : 0);
     a.err = dev.err;
+    if (stall_cycles > 0) {
+      a.stall = 1;
+      a.wait_cycles = stall_cycles;
+    }
     e = p.pair ? tc_pair_launch(p.epi, p.qres, &qmap, &xmap, a, s) : tc_launch(p.epi, p.qres, &qmap, &xmap, a, s);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 search launch");
   }
@@ -504,6 +516,13 @@ cvs_status cvs_poll_device_error(int device, int* code) {
   return CVS_OK;
 }
 
+cvs_status cvs_debug_stall_next_search(int64_t wait_cycles) {
+  if (wait_cycles < 1000 || wait_cycles > (int64_t{1} << 40))
+    return fail(CVS_ERR_INVALID_ARGUMENT, "wait_cycles must be in 1000 .. 2^40 (got %lld)", (long long)wait_cycles);
+  g_stall_cycles = wait_cycles;
+  return CVS_OK;
+}
+
 cvs_status cvs_set_profile_events(void* start_event, void* stop_event) {
   g_prof_start = static_cast<cudaEvent_t>(start_event);
   g_prof_stop = static_cast<cudaEvent_t>(stop_event);
@@ -579,7 +598,12 @@ extern "C" cvs_status cvs_fused_topk_noalloc(const void* q_f16, int64_t b, const
   if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p)) != CVS_OK) return st;
   if (p.ws_bytes > kNoAllocScratchBytes && plan_chunks == 0) {
     // Automatic plan too large: the most corpus segments whose candidate lists
-    // fit (list bytes grow with the segment count).
+    // fit. The binary search assumes the workspace size never shrinks as the
+    // segment count grows: it is b * lists * cap * 8 bytes plus fixed parts,
+    // lists = segments x a per-epilogue constant, and cap depends on k alone.
+    // A planner change that let the epilogue (its list count or cap) depend on
+    // the segment count would break that; the check after the search catches
+    // it and falls back to scanning down one segment count at a time.
     int lo = 1, hi = p.segs - 1, best = 0;
     while (lo <= hi) {
       const int mid = (lo + hi) / 2;
@@ -590,6 +614,16 @@ extern "C" cvs_status cvs_fused_topk_noalloc(const void* q_f16, int64_t b, const
         lo = mid + 1;
       } else {
         hi = mid - 1;
+      }
+    }
+    if (best > 0 && best + 1 < p.segs) {
+      Plan t;
+      if ((st = plan_fused(b, n, d_pad, k, best + 1, dev, &t)) != CVS_OK) return st;
+      if (t.ws_bytes <= kNoAllocScratchBytes) {  // not monotonic after all: scan down instead
+        for (best = p.segs - 1; best > 0; --best) {
+          if ((st = plan_fused(b, n, d_pad, k, best, dev, &t)) != CVS_OK) return st;
+          if (t.ws_bytes <= kNoAllocScratchBytes) break;
+        }
       }
     }
     if (best > 0) {

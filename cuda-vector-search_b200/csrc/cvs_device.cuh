@@ -67,14 +67,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete. Returns false (after
 // recording kErrTimeout|site in *err and raising *abort) if it does not complete
 // within kWaitCycles, or if another role already raised *abort.
+// `limit` (SM clocks) is kWaitCycles except where a test shortens it.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* err, int site) {
+                                          int* err, int site, long long limit = kWaitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort = 1;
       report_error(err, kErrTimeout | site);
       return false;

@@ -74,6 +74,11 @@ struct TcArgs {
   int dry;            // tiles each CTA reads dry first (0 or kDryTiles)
   void* scores_out;   // [b][n] fp32/fp16 for the store epilogues
   int* err;           // device error word
+  // Failure-path test hook (one-CTA kernel only; cvs_debug_stall_next_search):
+  // stall != 0 makes the producer claim and load nothing, and wait_cycles > 0
+  // replaces the ~1 s limit of the kernel's waits, so every wait runs out.
+  long long wait_cycles;
+  int stall;
 };
 
 // Candidate lists each (query, segment) produces with this epilogue (one per

@@ -61,7 +61,7 @@ __device__ __forceinline__ void log_put_remote(uint32_t log_cluster, int iter, u
 // Waits (bounded, like mbar_wait) until the slot of iteration `iter` carries
 // that iteration, and returns its value in *v.
 __device__ __forceinline__ bool log_get(const uint64_t* log, int iter, uint32_t* v, volatile int* abort,
-                                        int* err, int site) {
+                                        int* err, int site, long long limit = kWaitCycles) {
   const uint32_t addr = smem_u32(log + (iter % kLogSlots));
   long long t0 = 0;
   for (int spin = 0;; ++spin) {
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool log_get(const uint64_t* log, int iter, uint32_t*
     }
     if (spin == 0) t0 = clock64();
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort = 1;
       report_error(err, kErrTimeout | site);
       return false;

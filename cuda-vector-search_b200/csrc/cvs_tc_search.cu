@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
   int nd = 0;  // dry tiles (see kDryTiles): the first nd claimed tiles, revisited at the end
   if constexpr (Epi::kTops) nd = Epi::dry_ok(a) ? a.dry : 0;
   volatile int* abort = sh.abort_flag();
+  const long long wlim = a.wait_cycles > 0 ? a.wait_cycles : kWaitCycles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kS; ++s) {
@@ -158,7 +159,9 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
-    if (elect_one_lane()) {
+    // (a.stall: a test of the failure path -- nothing is claimed, logged or
+    // loaded, so the other roles' waits run out.)
+    if (elect_one_lane() && !a.stall) {
       const uint64_t pol_x = l2_policy_evict_first();
       const uint64_t pol_q = l2_policy_evict_last();
       const int qrow0 = qt * kTcM;
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         for (int ks = 0; ks < a.ksl; ++ks, ++it) {
           const int s = it % kS;
           const uint32_t ph = (it / kS) & 1;
-          if (!mbar_wait(sh.empty(s), ph ^ 1, abort, a.err, 1)) {
+          if (!mbar_wait(sh.empty(s), ph ^ 1, abort, a.err, 1, wlim)) {
             ok = false;
             break;
           }
@@ -202,18 +205,18 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     if (elect_one_lane()) {
       const uint32_t idesc = idesc_f16_f32(kTcM, kTcN);
       bool ok = true;
-      if (QRES) ok = mbar_wait(sh.qfull(), 0, abort, a.err, 2);
+      if (QRES) ok = mbar_wait(sh.qfull(), 0, abort, a.err, 2, wlim);
       int it = 0;
       for (int t = 0; ok; ++t) {
         uint32_t v;
-        if (!log_get(sh.log(), t, &v, abort, a.err, 6)) {
+        if (!log_get(sh.log(), t, &v, abort, a.err, 6, wlim)) {
           ok = false;
           break;
         }
         if (v == kLogEnd) break;
         const int acc = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
-        if (!mbar_wait(sh.tempty(acc), (use & 1) ^ 1, abort, a.err, 3)) {
+        if (!mbar_wait(sh.tempty(acc), (use & 1) ^ 1, abort, a.err, 3, wlim)) {
           ok = false;
           break;
         }
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         for (int ks = 0; ks < a.ksl; ++ks, ++it) {
           const int s = it % kS;
           const uint32_t ph = (it / kS) & 1;
-          if (!mbar_wait(sh.full(s), ph, abort, a.err, 4)) {
+          if (!mbar_wait(sh.full(s), ph, abort, a.err, 4, wlim)) {
             ok = false;
             break;
           }
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     for (int t = 0;; ++t) {
       uint32_t v = 0;
       int got = 1;
-      if (lane == 0) got = log_get(sh.log(), t, &v, abort, a.err, 7) ? 1 : 0;
+      if (lane == 0) got = log_get(sh.log(), t, &v, abort, a.err, 7, wlim) ? 1 : 0;
       got = __shfl_sync(kFullMask, got, 0);
       v = __shfl_sync(kFullMask, v, 0);
       if (!got) {
@@ -281,7 +284,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         // other lists' refresh after the last dry tile has landed.
         if (qvalid && (t != nd || nd == 0)) fresh = load_bound(a.gthr + q);
       }
-      if (!mbar_wait(sh.tfull(acc), use & 1, abort, a.err, 5)) {
+      if (!mbar_wait(sh.tfull(acc), use & 1, abort, a.err, 5, wlim)) {
         ok = false;
         break;
       }

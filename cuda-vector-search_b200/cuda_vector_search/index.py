@@ -258,9 +258,15 @@ class Index:
 
     @classmethod
     def load(cls, path, metric: str | None = None, device=None) -> "Index":
+        """Read a file written by ``save`` (reference index.py:148-155).
+
+        The ``.npy`` is memory-mapped, not read whole: the ingest stages it to the
+        device in 2^18-row chunks, so host memory holds one chunk at a time.
+        """
         path = Path(path)
         if metric is None:
             side = Path(str(path) + ".json")
             metric = json.loads(side.read_text())["metric"] if side.exists() else "cosine"
-        x = torch.from_numpy(np.load(path))
+        # Copy-on-write mapping: writable for torch.from_numpy, never written back.
+        x = np.load(path, mmap_mode="c")
         return cls(x, metric=metric, device=device, copy=False)

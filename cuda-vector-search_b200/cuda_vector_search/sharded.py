@@ -18,20 +18,25 @@ rows and the merge compares (score, global id) keys.
 
 from __future__ import annotations
 
+import json
 from dataclasses import dataclass
+from pathlib import Path
 from typing import Callable
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
 from . import _ext
-from .index import MAX_FUSED_K, Index
+from .index import MAX_FUSED_K, Index, _to_tensor
 
 
-def all_gather_stacked(t: torch.Tensor, group=None) -> torch.Tensor:
-    """[world, *t.shape] gather of ``t`` from every rank (same shape everywhere)."""
+def all_gather_stacked(t: torch.Tensor, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[world, *t.shape] gather of ``t`` from every rank (same shape everywhere),
+    into ``out`` when given."""
     world = dist.get_world_size(group)
-    out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+    if out is None:
+        out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(out, t.contiguous(), group=group)
     else:
@@ -72,15 +77,27 @@ def _block_views(block: torch.Tensor, b: int, k: int):
 
 
 def cuda_shard_ops(index: Index) -> ShardOps:
-    """Operations backed by this package's kernels for one rank's Index."""
+    """Operations backed by this package's kernels for one rank's Index.
+
+    The search workspace is allocated once per (batch, k) and reused by later
+    searches of that shape, in stream order on the current stream.
+    """
     mod = _ext.load()
+    workspaces: dict = {}
+
+    def workspace(b, kk):
+        ws = workspaces.get((b, kk))
+        if ws is None:
+            ws = torch.empty(max(256, mod.workspace_size(b, len(index), index._x.shape[1], kk)),
+                             dtype=torch.uint8, device=index.device)
+            workspaces[(b, kk)] = ws
+        return ws
 
     def local_topk_into(queries, k, id_offset, v, i):
         q = index._prep_queries(queries)
         b = q.shape[0]
         kk = min(k, len(index))
-        ws = torch.empty(max(256, mod.workspace_size(b, len(index), index._x.shape[1], kk)),
-                         dtype=torch.uint8, device=index.device)
+        ws = workspace(b, kk)
         if kk == k:
             mod.fused_topk_into(q, index._x, kk, id_offset, v, i, ws)
         else:  # shard smaller than k: its kk results, then empty slots
@@ -106,6 +123,21 @@ def cuda_shard_ops(index: Index) -> ShardOps:
                     local_topk_into=local_topk_into)
 
 
+def load_shard_rows(path, rank: int, world: int, metric: str | None = None):
+    """(rows, first_row, metric) of shard ``rank`` of ``world`` of a file written
+    by ``Index.save``: the contiguous row range [n*rank//world, n*(rank+1)//world)
+    of the memory-mapped ``.npy`` (nothing is read until the rows are used) and
+    the metric from the ``<path>.json`` sidecar unless given."""
+    path = Path(path)
+    if metric is None:
+        side = Path(str(path) + ".json")
+        metric = json.loads(side.read_text())["metric"] if side.exists() else "cosine"
+    x = np.load(path, mmap_mode="c")  # copy-on-write: writable for torch, never written back
+    n = int(x.shape[0])
+    lo, hi = n * rank // world, n * (rank + 1) // world
+    return x[lo:hi], lo, metric
+
+
 class ShardedIndex:
     """Exact top-k over a corpus whose rows are split across the ranks of a group.
 
@@ -119,28 +151,69 @@ class ShardedIndex:
                  copy: bool = True, ops: ShardOps | None = None):
         if not dist.is_available() or not dist.is_initialized():
             raise RuntimeError("ShardedIndex needs an initialised torch.distributed process group")
+        if metric not in ("cosine", "ip"):
+            raise ValueError("metric must be 'cosine' or 'ip'")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         if ops is None:
             if shard_embeddings is None:
                 raise ValueError("shard_embeddings is required")
-            self.local = Index(shard_embeddings, metric=metric, device=device, copy=copy)
+            x = _to_tensor(shard_embeddings)
+            n_local = int(x.shape[0]) if x.dim() == 2 else 0
+            size_dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            if size_dev.type == "cuda" and size_dev.index is None:
+                size_dev = torch.device("cuda", torch.cuda.current_device())
+        else:
+            n_local, size_dev = ops.n_local, ops.device
+        # Shard sizes first, so that a rank with no rows makes EVERY rank raise
+        # the same error here instead of leaving the others blocked in a later
+        # collective until the process-group timeout.
+        sizes = all_gather_stacked(torch.tensor([n_local], dtype=torch.int64, device=size_dev), group)
+        sizes = [int(s) for s in sizes.flatten().tolist()]
+        if min(sizes) < 1:
+            raise ValueError(f"every rank must hold at least one row; shard sizes are {sizes}")
+        if sum(sizes) >= 2**31:
+            raise ValueError("a sharded corpus must have fewer than 2^31 rows in total")
+        if ops is None:
+            self.local = Index(x, metric=metric, device=device, copy=copy)
             ops = cuda_shard_ops(self.local)
         else:
             self.local = None
         self.ops = ops
         self.metric = metric
-        sizes = all_gather_stacked(torch.tensor([ops.n_local], dtype=torch.int64, device=ops.device), group)
-        sizes = [int(s) for s in sizes.flatten().tolist()]
         self.shard_sizes = sizes
         self.row_offset = sum(sizes[: self.rank])
         self.n_total = sum(sizes)
-        if self.n_total >= 2**31:
-            raise ValueError("a sharded corpus must have fewer than 2^31 rows in total")
+        self._buffers: dict = {}  # (b, k) -> (local block, gathered blocks), reused in stream order
+        # Optional profiling hook: four CUDA events recorded on the current stream
+        # before the local search, after it, after the all-gather and after the merge.
+        self.phase_events = None
+
+    @classmethod
+    def load(cls, path, metric: str | None = None, device=None, group=None, ops_factory=None) -> "ShardedIndex":
+        """Collective load of a file written by ``Index.save``: rank r of W maps the
+        ``.npy`` and ingests only its contiguous row range [n*r//W, n*(r+1)//W), in
+        2^18-row chunks, so no rank reads (or holds) more than its own rows.
+        ``ops_factory(rows)``, if given, builds the rank's ShardOps from its rows
+        (a numpy array) instead of a GPU Index."""
+        if not dist.is_available() or not dist.is_initialized():
+            raise RuntimeError("ShardedIndex needs an initialised torch.distributed process group")
+        rows, _, metric = load_shard_rows(path, dist.get_rank(group), dist.get_world_size(group), metric)
+        if ops_factory is not None:
+            return cls(metric=metric, group=group, ops=ops_factory(rows))
+        return cls(rows, metric=metric, device=device, group=group)
 
     def __len__(self) -> int:
         return self.n_total
+
+    def _block_pair(self, b: int, k: int, device):
+        bufs = self._buffers.get((b, k))
+        if bufs is None:
+            block = torch.empty(_block_bytes(b, k), dtype=torch.uint8, device=device)
+            gathered = torch.empty((self.world, block.numel()), dtype=torch.uint8, device=device)
+            bufs = self._buffers[(b, k)] = (block, gathered)
+        return bufs
 
     def search(self, queries, k: int = 10):
         k = int(k)
@@ -149,18 +222,28 @@ class ShardedIndex:
         k = min(k, self.n_total)
         if k > MAX_FUSED_K:
             raise ValueError(f"sharded search supports k <= {MAX_FUSED_K}")
+        ev = self.phase_events
+        if ev is not None:
+            ev[0].record()
         if self.ops.local_topk_into is not None:
             b = queries.shape[0] if getattr(queries, "ndim", 1) == 2 else 1
-            block = torch.empty(_block_bytes(b, k), dtype=torch.uint8, device=self.ops.device)
+            block, gathered = self._block_pair(b, k, self.ops.device)
             v, i = _block_views(block, b, k)
             self.ops.local_topk_into(queries, k, self.row_offset, v, i)
         else:
             v, i = self.ops.local_topk(queries, k, self.row_offset)
             b = v.shape[0]
-            block = torch.empty(_block_bytes(b, k), dtype=torch.uint8, device=v.device)
+            block, gathered = self._block_pair(b, k, v.device)
             bv, bi = _block_views(block, b, k)
             bv.copy_(v)
             bi.copy_(i)
-        gathered = all_gather_stacked(block, self.group)  # [W, block bytes], one collective
+        if ev is not None:
+            ev[1].record()
+        all_gather_stacked(block, self.group, out=gathered)  # [W, block bytes], one collective
+        if ev is not None:
+            ev[2].record()
         v_all, i_all = _block_views(gathered, b, k)
-        return self.ops.merge(v_all, i_all, k)
+        out = self.ops.merge(v_all, i_all, k)
+        if ev is not None:
+            ev[3].record()
+        return out

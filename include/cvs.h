@@ -145,6 +145,20 @@ cvs_status cvs_fused_topk_noalloc(const void* q_f16, int64_t b, const void* x_f1
 cvs_status cvs_poll_device_error(int device, int* code);
 
 /*
+ * Test hook for the failure path (no reference counterpart). Arms the next
+ * cvs_fused_topk call made on this host thread, and only that one. If its plan
+ * is the one-CTA tcgen05 kernel (2..128 queries, or 1 query with k > 32), that
+ * kernel's producer claims and loads no corpus tile and its pipeline waits give
+ * up after wait_cycles SM clocks instead of ~1 s, so every wait runs out: the
+ * kernel records kErrTimeout | site (0x100 | site) in the device error word,
+ * releases its tensor memory and returns; cvs_poll_device_error then reports
+ * CVS_ERR_DEVICE_TIMEOUT with that code, and the GPU stays usable. The armed
+ * call's results are undefined. Any other plan disarms the hook and returns
+ * CVS_ERR_INVALID_ARGUMENT. wait_cycles: 1000 .. 2^40.
+ */
+cvs_status cvs_debug_stall_next_search(int64_t wait_cycles);
+
+/*
  * Profiling hook: when both are non-NULL (cudaEvent_t handles), every
  * cvs_fused_topk call records start_event just before its main search kernel
  * and stop_event right after it, on the call's stream. NULL disables. Process

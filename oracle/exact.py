@@ -82,10 +82,25 @@ def merge_topk(v_lists, i_lists, k: int):
 
 def exact_topk(queries: np.ndarray, corpus: np.ndarray, k: int, chunk: int = CHUNK):
     """reference.py:18-34 in numpy: fp32 scores, chunked top-k with running merge."""
+    blocks = ((start, corpus[start : start + chunk]) for start in range(0, corpus.shape[0], chunk))
+    return exact_topk_blocks(queries, blocks, k)
+
+
+def exact_topk_blocks(queries: np.ndarray, blocks, k: int):
+    """The same chunked search over corpus blocks supplied by the caller.
+
+    ``blocks`` yields ``(first_row, rows)`` pairs that together cover the corpus
+    (any block size, in any order); ``rows`` is converted to fp32. This lets a
+    checker stream a corpus that does not fit in host memory at once (e.g. from
+    device memory) through the same arithmetic as ``exact_topk``: per block fp32
+    scores and top-k with ids shifted by the block start, then the running merge
+    of reference.py:28-33. The result does not depend on the block size: ties are
+    ordered by id.
+    """
     q = np.asarray(queries, dtype=np.float32)
     best_v = best_i = None
-    for start in range(0, corpus.shape[0], chunk):
-        blk = np.asarray(corpus[start : start + chunk], dtype=np.float32)
+    for start, rows in blocks:
+        blk = np.asarray(rows, dtype=np.float32)
         s = q @ blk.T
         v, i = topk_rows(s, k, base=start)
         if best_v is None:
@@ -93,3 +108,31 @@ def exact_topk(queries: np.ndarray, corpus: np.ndarray, k: int, chunk: int = CHU
         else:
             best_v, best_i = merge_topk([best_v, v], [best_i, i], k)
     return best_v, best_i
+
+
+def compare_topk(got_v, got_i, ref_v, ref_i, k: int, atol: float = 1e-3, rel: float = 1e-5) -> dict:
+    """Checks a [b, k] search result against the oracle's top-(k+1) (top-k when k == n).
+
+    The acceptance rule of the fused path: every returned id is one of the
+    oracle's top-k ids, except where the oracle's k-th and (k+1)-th scores are
+    closer than ``rel`` (relative), and every returned score is within ``atol``
+    of the oracle's score at the same rank. Rows must come back best first.
+    Returns {"ok", "rows", "recall", "max_abs_err", "bad_rows"}.
+    """
+    got_v = np.asarray(got_v, dtype=np.float64)
+    got_i = np.asarray(got_i, dtype=np.int64)
+    ref_v = np.asarray(ref_v, dtype=np.float64)
+    ref_i = np.asarray(ref_i, dtype=np.int64)
+    b = got_v.shape[0]
+    hits = 0
+    bad = []
+    err = float(np.abs(got_v - ref_v[:, :k]).max()) if b else 0.0
+    for r in range(b):
+        want = set(ref_i[r, :k].tolist())
+        hit = len(want & set(got_i[r].tolist()))
+        hits += hit
+        tie = ref_v.shape[1] > k and abs(ref_v[r, k - 1] - ref_v[r, k]) < rel * max(abs(ref_v[r, k - 1]), 1e-30)
+        if (hit < k and not tie) or not (got_v[r, :-1] >= got_v[r, 1:]).all():
+            bad.append(r)
+    return {"ok": not bad and err <= atol, "rows": int(b), "recall": hits / max(1, b * k),
+            "max_abs_err": err, "bad_rows": bad[:8]}

@@ -62,3 +62,31 @@ def assert_topk_exact(got_v, got_i, q32, x32, ref_v, ref_i, k, atol=ATOL, rel=RE
         if not boundary_tie:
             missing = set(ref_i[r, :k].tolist()) - set(row.tolist())
             assert not missing, f"row {r}: ids {sorted(missing)[:5]} of the oracle top-{k} missing"
+
+
+class DeviceRows:
+    """The stored corpus of an index, read row by row for ``assert_topk_exact``.
+
+    Stands in for the host fp32 matrix at sizes that do not fit in host memory
+    at once: ``shape`` is [n, d] and ``rows[ids]`` copies the requested stored
+    fp16 rows from the device and widens them to fp32 (exact).
+    """
+
+    def __init__(self, x_dev, d: int):
+        self.x = x_dev
+        self.d = d
+        self.shape = (int(x_dev.shape[0]), d)
+
+    def __getitem__(self, ids):
+        import torch
+
+        t = torch.as_tensor(np.asarray(ids, dtype=np.int64), device=self.x.device)
+        return self.x.index_select(0, t).cpu()[:, : self.d].float().numpy()
+
+
+def device_blocks(x_dev, d: int, rows: int = 1 << 19):
+    """(first_row, fp32 host rows) blocks of a stored device corpus, for
+    ``oracle.exact_topk_blocks``: fp16 rows copied to the host, widened to fp32."""
+    for start in range(0, int(x_dev.shape[0]), rows):
+        blk = x_dev[start : start + rows].cpu()
+        yield start, blk[:, :d].float().numpy()

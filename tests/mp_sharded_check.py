@@ -1,5 +1,5 @@
-"""torchrun helper for test_sharded_gpu.py: ShardedIndex over NCCL equals a
-single-GPU Index on the same global corpus (rank 0 checks)."""
+"""torchrun helper for test_sharded_gpu.py: ShardedIndex over NCCL matches the
+CPU oracle on the global corpus and equals a single-GPU Index (rank 0 checks)."""
 
 import os
 from datetime import timedelta
@@ -25,11 +25,18 @@ def main():
     v, i = idx.search(q.to(dev), k)
     v2, i2 = idx.search(q.to(dev), 1024)
     if rank == 0:
-        ref_v, ref_i = cvs.Index(x.to(dev), metric="cosine").search(q.to(dev), k)
-        assert torch.equal(i, ref_i), "ids differ"
-        assert torch.allclose(v, ref_v, atol=1e-6, rtol=0)
-        ref_v2, ref_i2 = cvs.Index(x.to(dev), metric="cosine").search(q.to(dev), 1024)
-        assert torch.equal(i2, ref_i2) and torch.allclose(v2, ref_v2, atol=1e-6, rtol=0)
+        from helpers import assert_topk_exact
+        from oracle import exact_topk
+
+        whole = cvs.Index(x.to(dev), metric="cosine")
+        x32 = whole.embeddings.float().cpu().numpy()  # the stored (normalised) global corpus
+        q32 = whole._prep_queries(q.to(dev))[:, :d].float().cpu().numpy()
+        for kk, (vv, ii) in ((k, (v, i)), (1024, (v2, i2))):
+            ov, oi = exact_topk(q32, x32, kk + 1)
+            assert_topk_exact(vv.cpu().numpy(), ii.cpu().numpy(), q32, x32, ov, oi, kk)
+            ref_v, ref_i = whole.search(q.to(dev), kk)
+            assert torch.equal(ii, ref_i), "ids differ from the single-GPU index"
+            assert torch.allclose(vv, ref_v, atol=1e-6, rtol=0)
         print("SHARDED OK", flush=True)
     dist.barrier()
     dist.destroy_process_group()

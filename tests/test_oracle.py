@@ -83,3 +83,46 @@ def test_normalize_matches_reference(case):
     diff = np.abs(ours.view(np.int16).astype(np.int32) - ref.numpy().view(np.int16).astype(np.int32))
     assert diff.max() <= 1  # at most one fp16 ulp
     assert (diff == 0).mean() > 0.9999
+
+
+def test_cpu_baseline_paths_agree_with_the_oracle():
+    """The three timed CPU paths (oracle/cpu_paths.py) compute the reference's
+    fp32 search: same top-k as the oracle on the same stored vectors."""
+    from oracle import compare_topk, index_cpu_search, numpy_search, time_call, torch_exact_topk_fp32
+
+    x, q = make(30000, 128, 6, seed=3)
+    x32, q32 = x.float(), q.float()
+    ref_v, ref_i = exact_topk(q.numpy(), x.numpy(), 11)
+    for v, i in (index_cpu_search(q32, x32, 10), torch_exact_topk_fp32(q32, x32, 10, chunk=7000),
+                 numpy_search(q32.numpy(), x32.numpy(), 10)):
+        res = compare_topk(np.asarray(v), np.asarray(i), ref_v, ref_i, 10, atol=1e-5)
+        assert res["ok"] and res["recall"] == 1.0, res
+    ms, reps = time_call(lambda: numpy_search(q32.numpy(), x32.numpy(), 10), target_s=0.05)
+    assert ms > 0 and reps >= 3
+
+
+def test_streamed_blocks_equal_one_shot():
+    """exact_topk_blocks over uneven blocks in any order equals exact_topk."""
+    from oracle import exact_topk_blocks
+
+    x, q = make(20000, 64, 5, seed=8)
+    xs = x.numpy()
+    bounds = [0, 777, 5000, 5001, 13000, 20000]
+    blocks = [(bounds[j], xs[bounds[j]:bounds[j + 1]]) for j in range(len(bounds) - 1)][::-1]
+    v1, i1 = exact_topk_blocks(q.numpy(), iter(blocks), 15)
+    v2, i2 = exact_topk(q.numpy(), xs, 15)
+    assert (i1 == i2).all() and np.abs(v1 - v2).max() < 1e-6
+
+
+def test_compare_topk_flags_a_wrong_id():
+    from oracle import compare_topk
+
+    x, q = make(5000, 64, 4, seed=2)
+    ref_v, ref_i = exact_topk(q.numpy(), x.numpy(), 11)
+    got_v, got_i = ref_v[:, :10].copy(), ref_i[:, :10].copy()
+    assert compare_topk(got_v, got_i, ref_v, ref_i, 10)["ok"]
+    got_i[2, 9] = ref_i[2, 10] + 1 if ref_i[2, 10] + 1 not in ref_i[2] else 4999
+    assert compare_topk(got_v, got_i, ref_v, ref_i, 10)["bad_rows"] == [2]
+    got_i[2, 9] = ref_i[2, 9]
+    got_v[1, 0] += 0.01
+    assert not compare_topk(got_v, got_i, ref_v, ref_i, 10)["ok"]

@@ -136,6 +136,15 @@ def test_one_dim_query_and_large_k(cvs):
     assert_topk_exact(v.cpu().numpy(), i.cpu().numpy(), q32, x32, ref_v, ref_i, 400)
     v, i = index.search(q.cuda(), 1500)  # beyond the fused limit -> twopass
     assert i.shape == (1, 1500)
+    # twopass keeps fp16 scores: the reference contract at its 2e-3 tolerance
+    # (test_search.py:72-80), against the fp32 oracle.
+    ref_v, _ = exact_topk(q32, x32, 1500)
+    v, i = v.cpu().numpy(), i.cpu().numpy()
+    ts = true_scores(q32, x32, i)
+    assert np.abs(v - ts).max() <= 2e-3
+    assert (ts >= ref_v[:, -1:] - 2e-3).all()
+    assert (v[:, :-1] >= v[:, 1:] - 1e-6).all()
+    assert len(set(i[0].tolist())) == 1500
 
 
 def test_fused_plan_overrides(cvs):
@@ -145,10 +154,14 @@ def test_fused_plan_overrides(cvs):
     mod = _ext.load()
     c, index, q = build(cvs, "plan_overrides")
     qq = index._prep_queries(q)
+    x32, q32 = stored(index), prepped(index, q)
+    ref_v, ref_i = exact_topk(q32, x32, 11)
     base_v, base_i = index.search(q, 10, method="fused")
-    for bq, chunks in [(16, 1), (32, 7), (64, 1000)]:
+    assert_topk_exact(base_v.cpu().numpy(), base_i.cpu().numpy(), q32, x32, ref_v, ref_i, 10)
+    for bq, chunks in [(16, 1), (32, 7), (64, 1000), (256, 3)]:
         v, i, plan = mod.fused_topk(qq, index._x, 10, bq, chunks)
         assert plan.tolist()[0] == bq
+        assert_topk_exact(v.cpu().numpy(), i.cpu().numpy(), q32, x32, ref_v, ref_i, 10)
         assert torch.allclose(v, base_v, atol=1e-5)
         assert torch.equal(i, base_i)
 

@@ -75,9 +75,13 @@ def _worker(rank, world, port, case, out):
 
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=case.get("timeout", 60)))
         x, q = _corpus(**case["data"])
-        bounds = case["bounds"]
-        shard = x[bounds[rank]:bounds[rank + 1]]
-        idx = ShardedIndex(ops=_cpu_ops(shard))
+        if case.get("load"):
+            # Each rank maps the saved file and takes only its own row range.
+            idx = ShardedIndex.load(case["load"], ops_factory=lambda rows: _cpu_ops(np.asarray(rows)))
+        else:
+            bounds = case["bounds"]
+            shard = x[bounds[rank]:bounds[rank + 1]]
+            idx = ShardedIndex(ops=_cpu_ops(shard))
         if case.get("fail_rank") == rank:
             raise SystemExit(3)  # this rank leaves before the collective search
         v, i = idx.search(q.astype(np.float32), case["k"])
@@ -133,3 +137,32 @@ def test_a_rank_that_leaves_makes_the_others_fail_not_hang():
     res = _run(case)
     assert res[1][0] == "exited"
     assert res[0][0] == "error"  # the collective search raised after the short timeout
+
+
+def test_sharded_load_maps_each_ranks_row_range(tmp_path):
+    """ShardedIndex.load: rank r of W ingests rows [n*r//W, n*(r+1)//W) of one
+    saved .npy (the format Index.save writes); the global result equals the
+    oracle on the whole file."""
+    data = dict(n=3001, d=48, b=5, seed=4)
+    x, q = _corpus(**data)
+    path = tmp_path / "corpus.npy"
+    np.save(path, x)
+    (tmp_path / "corpus.npy.json").write_text('{"metric": "ip", "dim": 48, "n": 3001}')
+    res = _run(dict(data=data, load=str(path), k=17))
+    ref_v, ref_i = exact_topk(q.astype(np.float32), x, 17)
+    for rank, lo in ((0, 0), (1, 1500)):
+        status, offset, total, v, i = res[rank]
+        assert status == "ok", offset
+        assert offset == lo and total == 3001
+        np.testing.assert_allclose(v, ref_v, rtol=0, atol=1e-5)
+        assert (i == ref_i).all()
+
+
+def test_a_rank_without_rows_fails_on_every_rank():
+    """An empty shard is reported by every rank at construction (after the one
+    collective that gathers the shard sizes), not by a hang in a later search."""
+    case = dict(data=dict(n=1000, d=16, b=2, seed=3), bounds=(0, 0, 1000), k=5, timeout=20)
+    res = _run(case)
+    for rank in (0, 1):
+        assert res[rank][0] == "error"
+        assert "at least one row" in res[rank][1]

@@ -2,9 +2,11 @@
 
 * Simulated on one GPU: the corpus is split into S pseudo-shards, each searched
   with its global row offset (fused_topk_into), the [S, b, k] lists merged with
-  merge_lists; the result must equal the unsharded search exactly.
+  merge_lists; the result must match the CPU oracle on the global corpus and
+  equal the unsharded search exactly.
 * Real ranks: when at least two GPUs are visible, tests/mp_sharded_check.py runs
-  under torchrun with NCCL and compares ShardedIndex with a single-GPU Index.
+  under torchrun with NCCL and compares ShardedIndex with the CPU oracle on the
+  global corpus and with a single-GPU Index.
 """
 
 import os
@@ -14,6 +16,9 @@ from pathlib import Path
 
 import pytest
 import torch
+
+from helpers import assert_topk_exact
+from oracle import exact_topk
 
 pytestmark = pytest.mark.gpu
 
@@ -55,6 +60,12 @@ def test_simulated_sharding_equals_unsharded(mod, n, d, b, k, shards):
         vs.append(v)
         ids.append(i)
     mv, mi = mod.merge_lists(torch.stack(vs).contiguous(), torch.stack(ids).contiguous(), k)
+    # Against the CPU oracle on the stored (normalised) global corpus ...
+    x32 = full.embeddings.float().cpu().numpy()
+    q32 = full._prep_queries(q)[:, :d].float().cpu().numpy()
+    ov, oi = exact_topk(q32, x32, min(k + 1, n))
+    assert_topk_exact(mv.cpu().numpy(), mi.cpu().numpy(), q32, x32, ov, oi, k)
+    # ... and bit for bit against the unsharded search.
     assert torch.equal(mi, ref_i)
     assert torch.allclose(mv, ref_v, atol=1e-6, rtol=0)
 
@@ -70,3 +81,44 @@ def test_nccl_ranks_match_single_gpu():
     res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=360)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "SHARDED OK" in res.stdout
+
+
+def test_save_then_load_whole_and_per_shard_ranges(mod, tmp_path):
+    """Index.save, then (a) Index.load, which maps the .npy and stages it in
+    chunks, and (b) the per-rank row ranges ShardedIndex.load ingests
+    (load_shard_rows), searched as pseudo-shards on this GPU and merged: both
+    match the CPU oracle on the saved corpus."""
+    import numpy as np
+
+    import cuda_vector_search as cvs
+    from cuda_vector_search.sharded import load_shard_rows
+
+    g = torch.Generator().manual_seed(11)
+    n, d, b, k, shards = 300_001, 200, 40, 25, 3  # > one 2^18-row staging chunk, ragged ranges
+    x = torch.randn(n, d, generator=g).half()
+    q = torch.randn(b, d, generator=g).half().cuda()
+    path = tmp_path / "corpus.npy"
+    cvs.Index(x.cuda(), metric="cosine").save(path)
+    saved = np.load(path)
+    whole = cvs.Index.load(path)
+    assert whole.metric == "cosine" and len(whole) == n and whole.dim == d
+    q32 = whole._prep_queries(q)[:, :d].float().cpu().numpy()
+    x32 = whole.embeddings.float().cpu().numpy()
+    ov, oi = exact_topk(q32, x32, k + 1)
+    v, i = whole.search(q, k)
+    assert_topk_exact(v.cpu().numpy(), i.cpu().numpy(), q32, x32, ov, oi, k)
+    vs, ids = [], []
+    for r in range(shards):
+        rows, lo, metric = load_shard_rows(path, r, shards)
+        assert lo == n * r // shards and metric == "cosine"
+        assert np.array_equal(np.asarray(rows), saved[lo:lo + rows.shape[0]])
+        part = cvs.Index(rows, metric=metric)
+        pv = torch.empty(b, k, device="cuda")
+        pi = torch.empty(b, k, dtype=torch.int64, device="cuda")
+        ws = torch.empty(max(256, mod.workspace_size(b, len(part), part._x.shape[1], k)), dtype=torch.uint8,
+                         device="cuda")
+        mod.fused_topk_into(part._prep_queries(q), part._x, k, lo, pv, pi, ws)
+        vs.append(pv)
+        ids.append(pi)
+    mv, mi = mod.merge_lists(torch.stack(vs).contiguous(), torch.stack(ids).contiguous(), k)
+    assert_topk_exact(mv.cpu().numpy(), mi.cpu().numpy(), q32, x32, ov, oi, k)
