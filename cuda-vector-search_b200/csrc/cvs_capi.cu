@@ -193,8 +193,10 @@ void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks, int epi, i
   p->segs = (p->ntiles + p->tiles_per_seg - 1) / p->tiles_per_seg;
 }
 
+// own_queries: the search ingests its queries itself (cvs_search), into a
+// buffer of whole query tiles at the end of the workspace.
 cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const DeviceInfo& dev,
-                      Plan* p, int bq = 0) {
+                      Plan* p, int bq = 0, bool own_queries = false) {
   if (k < 1 || k > CVS_MAX_FUSED_K)
     return fail(CVS_ERR_INVALID_ARGUMENT, "fused top-k supports 1 <= k <= %d (got %d)", CVS_MAX_FUSED_K, k);
   if (k > n) return fail(CVS_ERR_INVALID_ARGUMENT, "k (%d) must not exceed the corpus size (%lld)", k, (long long)n);
@@ -213,6 +215,11 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->clear_bytes = static_cast<size_t>(b) * 4 * (1 + p->lists);
     p->bound_bytes = round_up(p->clear_bytes, kWsAlign);
     p->ws_bytes = p->bound_bytes + round_up(static_cast<size_t>(b) * p->lists * p->cap * 8, kWsAlign);
+    if (own_queries) {
+      p->qpad_rows = static_cast<int>(b);
+      p->qpad_offset = p->ws_bytes;
+      p->ws_bytes += round_up(static_cast<size_t>(b) * d_pad * 2, kWsAlign);
+    }
     return CVS_OK;
   }
   p->gemv = false;
@@ -246,7 +253,7 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
   // on every load, which costs up to a fifth of the kernel time at small
   // batches. Such batches are copied into a zero-padded buffer of whole tiles.
   const int tile_rows = p->pair ? 2 * kTcM : kTcM;
-  if (!p->qres && b % tile_rows != 0) {
+  if (own_queries || (!p->qres && b % tile_rows != 0)) {
     p->qpad_rows = p->qtiles * tile_rows;
     p->qpad_offset = p->ws_bytes;
     p->ws_bytes += round_up(static_cast<size_t>(p->qpad_rows) * d_pad * 2, kWsAlign);
@@ -254,103 +261,35 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
   return CVS_OK;
 }
 
-}  // namespace
-}  // namespace cvs
-
-using namespace cvs;
-
-extern "C" {
-
-const char* cvs_last_error(void) { return g_last_error.c_str(); }
-
-int cvs_abi_version(void) { return CVS_ABI_VERSION; }
-
-int cvs_pad_width(int d) { return d <= 0 ? 0 : (d + CVS_PAD - 1) / CVS_PAD * CVS_PAD; }
-
-cvs_status cvs_ingest(const void* src, int src_dtype, int64_t n, int d, int64_t src_row_stride,
-                      int d_pad, int cosine, void* dst_f16, void* stream) {
-  if (n < 0) return fail(CVS_ERR_INVALID_ARGUMENT, "row count must be >= 0");
-  if (n == 0) return CVS_OK;
-  if (!src || !dst_f16) return fail(CVS_ERR_INVALID_ARGUMENT, "null source or destination");
-  if (d < 1 || d > 2048) return fail(CVS_ERR_INVALID_ARGUMENT, "width must be in 1 .. 2048 (got %d)", d);
-  if (d_pad < d || d_pad % CVS_PAD != 0)
-    return fail(CVS_ERR_INVALID_ARGUMENT, "d_pad (%d) must be a multiple of 64 and >= d (%d)", d_pad, d);
-  if (src_row_stride < d) return fail(CVS_ERR_INVALID_ARGUMENT, "source row stride smaller than the width");
-  if (src_dtype < CVS_F32 || src_dtype > CVS_F64) return fail(CVS_ERR_INVALID_ARGUMENT, "unknown source dtype %d", src_dtype);
-  if (src == dst_f16 && !(src_dtype == CVS_F16 && d == d_pad && src_row_stride == d_pad))
-    return fail(CVS_ERR_INVALID_ARGUMENT, "in-place ingest needs fp16 input with d == d_pad == stride");
-  DeviceInfo dev;
-  cvs_status st = device_info(&dev);
-  if (st != CVS_OK) return st;
-  cudaError_t e = ingest_launch(src, src_dtype, n, d, src_row_stride, d_pad, cosine,
-                                static_cast<__half*>(dst_f16), dev.sms, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "ingest launch");
-  return CVS_OK;
-}
-
-cvs_status cvs_fused_topk_workspace_size(int64_t b, int64_t n, int d_pad, int k, int plan_bq,
-                                         int plan_chunks, size_t* bytes) {
-  (void)plan_bq;
-  if (!bytes) return fail(CVS_ERR_INVALID_ARGUMENT, "bytes must not be null");
-  *bytes = 0;
-  if (b < 0 || b >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "query count out of range");
-  if (n < 1 || n >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "corpus must have 1 .. 2^31-1 rows");
-  if (d_pad < CVS_PAD || d_pad % CVS_PAD != 0) return fail(CVS_ERR_INVALID_ARGUMENT, "width must be a multiple of 64");
-  if (b == 0) return CVS_OK;
-  DeviceInfo dev;
-  cvs_status st = device_info(&dev);
-  if (st != CVS_OK) return st;
-  Plan p;
-  st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p, plan_bq);
-  if (st != CVS_OK) return st;
-  *bytes = p.ws_bytes;
-  return CVS_OK;
-}
-
-cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64_t n, int d_pad,
-                          int k, int64_t id_offset, float* out_scores, int64_t* out_ids,
-                          void* workspace, size_t workspace_bytes, int plan_bq, int plan_chunks,
-                          int64_t* plan_out, void* stream) {
-  cvs_status st = check_pair(q_f16, b, x_f16, n, d_pad);
-  if (st != CVS_OK) return st;
-  DeviceInfo dev;
-  if ((st = device_info(&dev)) != CVS_OK) return st;
-  Plan p;
-  if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p, plan_bq)) != CVS_OK) return st;
-  if (plan_out) {
-    plan_out[0] = plan_bq > 0 ? plan_bq : (p.gemv ? static_cast<int64_t>(b) : static_cast<int64_t>(p.pair ? 2 * kTcM : kTcM));
-    plan_out[1] = p.segs;
-  }
-  if (b == 0) return CVS_OK;
-  const int64_t stall_cycles = g_stall_cycles;
-  g_stall_cycles = 0;  // one call only
-  if (stall_cycles > 0 && (p.gemv || p.pair))
-    return fail(CVS_ERR_INVALID_ARGUMENT, "the stall test hook needs a one-CTA tcgen05 plan (2..128 queries)");
+cvs_status check_outputs(const Plan& p, float* out_scores, int64_t* out_ids, void* workspace,
+                         size_t workspace_bytes) {
   if (!out_scores || !out_ids) return fail(CVS_ERR_INVALID_ARGUMENT, "null output pointer");
   if (!workspace || workspace_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) % kWsAlign) != 0)
     return fail(CVS_ERR_WORKSPACE, "workspace of %zu bytes (256-byte aligned) required, got %zu at %p",
                 p.ws_bytes, workspace_bytes, workspace);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return CVS_OK;
+}
+
+// Launches the search kernel and the merge for a planned call whose queries are
+// readable at q_tiles (padded as the plan says) and whose workspace is cleared
+// (by a kernel already enqueued on the stream).
+cvs_status launch_search(const Plan& p, const DeviceInfo& dev, const void* q_tiles, int64_t b, const void* x_f16,
+                         int64_t n, int d_pad, int k, int64_t id_offset, float* out_scores, int64_t* out_ids,
+                         void* workspace, cudaStream_t s) {
+  const int64_t stall_cycles = g_stall_cycles;
+  g_stall_cycles = 0;  // one call only
+  if (stall_cycles > 0 && (p.gemv || p.pair))
+    return fail(CVS_ERR_INVALID_ARGUMENT, "the stall test hook needs a one-CTA tcgen05 plan (2..128 queries)");
   uint32_t* bounds = static_cast<uint32_t*>(workspace);
   uint64_t* part = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + p.bound_bytes);
   const bool prof = g_prof_start && g_prof_stop;
+  cvs_status st;
   cudaError_t e;
-  // The shared per-query bounds must start at "none" (0) on every call.
-  const void* q_tiles = q_f16;  // what the tensor map reads
-  if (p.qpad_rows > 0) {
-    void* qpad = static_cast<char*>(workspace) + p.qpad_offset;
-    if ((e = prepare_launch(bounds, round_up(p.clear_bytes, 4), q_f16, qpad, static_cast<int>(b), d_pad,
-                            p.qpad_rows, s)) != cudaSuccess)
-      return cuda_fail(e, "clearing the workspace and padding the queries");
-    q_tiles = qpad;
-  } else if (p.clear_bytes && (e = prepare_launch(bounds, round_up(p.clear_bytes, 4), nullptr, nullptr, 0,
-                                                   d_pad, 0, s)) != cudaSuccess)
-    return cuda_fail(e, "clearing the per-query bounds");
   if (prof && (e = cudaEventRecord(g_prof_start, s)) != cudaSuccess) return cuda_fail(e, "profile event");
   if (p.gemv) {
     GemvArgs a{};
     a.x = static_cast<const __half*>(x_f16);
-    a.q = static_cast<const __half*>(q_f16);
+    a.q = static_cast<const __half*>(q_tiles);
     a.b = static_cast<int>(b);
     a.n = static_cast<int>(n);
     a.d_pad = d_pad;
@@ -422,6 +361,138 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
   m.err = dev.err;
   if ((e = merge_keys_launch(m, s)) != cudaSuccess) return cuda_fail(e, "merge launch");
   return CVS_OK;
+}
+
+
+}  // namespace
+}  // namespace cvs
+
+using namespace cvs;
+
+extern "C" {
+
+const char* cvs_last_error(void) { return g_last_error.c_str(); }
+
+int cvs_abi_version(void) { return CVS_ABI_VERSION; }
+
+int cvs_pad_width(int d) { return d <= 0 ? 0 : (d + CVS_PAD - 1) / CVS_PAD * CVS_PAD; }
+
+cvs_status cvs_ingest(const void* src, int src_dtype, int64_t n, int d, int64_t src_row_stride,
+                      int d_pad, int cosine, void* dst_f16, void* stream) {
+  if (n < 0) return fail(CVS_ERR_INVALID_ARGUMENT, "row count must be >= 0");
+  if (n == 0) return CVS_OK;
+  if (!src || !dst_f16) return fail(CVS_ERR_INVALID_ARGUMENT, "null source or destination");
+  if (d < 1 || d > 2048) return fail(CVS_ERR_INVALID_ARGUMENT, "width must be in 1 .. 2048 (got %d)", d);
+  if (d_pad < d || d_pad % CVS_PAD != 0)
+    return fail(CVS_ERR_INVALID_ARGUMENT, "d_pad (%d) must be a multiple of 64 and >= d (%d)", d_pad, d);
+  if (src_row_stride < d) return fail(CVS_ERR_INVALID_ARGUMENT, "source row stride smaller than the width");
+  if (src_dtype < CVS_F32 || src_dtype > CVS_F64) return fail(CVS_ERR_INVALID_ARGUMENT, "unknown source dtype %d", src_dtype);
+  if (src == dst_f16 && !(src_dtype == CVS_F16 && d == d_pad && src_row_stride == d_pad))
+    return fail(CVS_ERR_INVALID_ARGUMENT, "in-place ingest needs fp16 input with d == d_pad == stride");
+  DeviceInfo dev;
+  cvs_status st = device_info(&dev);
+  if (st != CVS_OK) return st;
+  cudaError_t e = ingest_launch(src, src_dtype, n, d, src_row_stride, d_pad, cosine,
+                                static_cast<__half*>(dst_f16), dev.sms, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "ingest launch");
+  return CVS_OK;
+}
+
+cvs_status cvs_fused_topk_workspace_size(int64_t b, int64_t n, int d_pad, int k, int plan_bq,
+                                         int plan_chunks, size_t* bytes) {
+  (void)plan_bq;
+  if (!bytes) return fail(CVS_ERR_INVALID_ARGUMENT, "bytes must not be null");
+  *bytes = 0;
+  if (b < 0 || b >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "query count out of range");
+  if (n < 1 || n >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "corpus must have 1 .. 2^31-1 rows");
+  if (d_pad < CVS_PAD || d_pad % CVS_PAD != 0) return fail(CVS_ERR_INVALID_ARGUMENT, "width must be a multiple of 64");
+  if (b == 0) return CVS_OK;
+  DeviceInfo dev;
+  cvs_status st = device_info(&dev);
+  if (st != CVS_OK) return st;
+  Plan p;
+  st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p, plan_bq);
+  if (st != CVS_OK) return st;
+  *bytes = p.ws_bytes;
+  return CVS_OK;
+}
+
+cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64_t n, int d_pad,
+                          int k, int64_t id_offset, float* out_scores, int64_t* out_ids,
+                          void* workspace, size_t workspace_bytes, int plan_bq, int plan_chunks,
+                          int64_t* plan_out, void* stream) {
+  cvs_status st = check_pair(q_f16, b, x_f16, n, d_pad);
+  if (st != CVS_OK) return st;
+  DeviceInfo dev;
+  if ((st = device_info(&dev)) != CVS_OK) return st;
+  Plan p;
+  if ((st = plan_fused(b, n, d_pad, k, plan_chunks, dev, &p, plan_bq)) != CVS_OK) return st;
+  if (plan_out) {
+    plan_out[0] = plan_bq > 0 ? plan_bq : (p.gemv ? static_cast<int64_t>(b) : static_cast<int64_t>(p.pair ? 2 * kTcM : kTcM));
+    plan_out[1] = p.segs;
+  }
+  if (b == 0) return CVS_OK;
+  if ((st = check_outputs(p, out_scores, out_ids, workspace, workspace_bytes)) != CVS_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t* bounds = static_cast<uint32_t*>(workspace);
+  cudaError_t e;
+  // The shared per-query bounds must start at "none" (0) on every call.
+  const void* q_tiles = q_f16;  // what the tensor map reads
+  if (p.qpad_rows > 0) {
+    void* qpad = static_cast<char*>(workspace) + p.qpad_offset;
+    if ((e = prepare_launch(bounds, round_up(p.clear_bytes, 4), q_f16, qpad, static_cast<int>(b), d_pad,
+                            p.qpad_rows, s)) != cudaSuccess)
+      return cuda_fail(e, "clearing the workspace and padding the queries");
+    q_tiles = qpad;
+  } else if (p.clear_bytes && (e = prepare_launch(bounds, round_up(p.clear_bytes, 4), nullptr, nullptr, 0,
+                                                   d_pad, 0, s)) != cudaSuccess)
+    return cuda_fail(e, "clearing the per-query bounds");
+  return launch_search(p, dev, q_tiles, b, x_f16, n, d_pad, k, id_offset, out_scores, out_ids, workspace, s);
+}
+
+cvs_status cvs_search_workspace_size(int64_t b, int64_t n, int d_pad, int k, size_t* bytes) {
+  if (!bytes) return fail(CVS_ERR_INVALID_ARGUMENT, "bytes must not be null");
+  *bytes = 0;
+  if (b < 0 || b >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "query count out of range");
+  if (n < 1 || n >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "corpus must have 1 .. 2^31-1 rows");
+  if (d_pad < CVS_PAD || d_pad % CVS_PAD != 0) return fail(CVS_ERR_INVALID_ARGUMENT, "width must be a multiple of 64");
+  if (b == 0) return CVS_OK;
+  DeviceInfo dev;
+  cvs_status st = device_info(&dev);
+  if (st != CVS_OK) return st;
+  Plan p;
+  if ((st = plan_fused(b, n, d_pad, k, 0, dev, &p, 0, true)) != CVS_OK) return st;
+  *bytes = p.ws_bytes;
+  return CVS_OK;
+}
+
+cvs_status cvs_search(const void* q_src, int src_dtype, int64_t b, int d, int64_t src_row_stride, int cosine,
+                      const void* x_f16, int64_t n, int d_pad, int k, int64_t id_offset, float* out_scores,
+                      int64_t* out_ids, void* workspace, size_t workspace_bytes, void* stream) {
+  if (b < 0 || b >= INT_MAX) return fail(CVS_ERR_INVALID_ARGUMENT, "query count %lld out of range", (long long)b);
+  if (b == 0) return CVS_OK;
+  if (!q_src) return fail(CVS_ERR_INVALID_ARGUMENT, "queries must not be null");
+  if (d < 1 || d > 2048) return fail(CVS_ERR_INVALID_ARGUMENT, "query width must be in 1 .. 2048 (got %d)", d);
+  if (d > d_pad) return fail(CVS_ERR_INVALID_ARGUMENT, "query width %d exceeds the corpus width %d", d, d_pad);
+  if (src_row_stride < d) return fail(CVS_ERR_INVALID_ARGUMENT, "query row stride smaller than the width");
+  if (src_dtype < CVS_F32 || src_dtype > CVS_F64) return fail(CVS_ERR_INVALID_ARGUMENT, "unknown query dtype %d", src_dtype);
+  // Queries are read by the ingest, not by TMA: only the corpus needs the
+  // alignment check (a stand-in 16-byte aligned query pointer passes it).
+  cvs_status st = check_pair(x_f16, b, x_f16, n, d_pad);
+  if (st != CVS_OK) return st;
+  DeviceInfo dev;
+  if ((st = device_info(&dev)) != CVS_OK) return st;
+  Plan p;
+  if ((st = plan_fused(b, n, d_pad, k, 0, dev, &p, 0, true)) != CVS_OK) return st;
+  if ((st = check_outputs(p, out_scores, out_ids, workspace, workspace_bytes)) != CVS_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // One launch converts, normalises and pads the queries into whole query
+  // tiles in the workspace and clears the bounds; the search kernel follows.
+  __half* qbuf = reinterpret_cast<__half*>(static_cast<char*>(workspace) + p.qpad_offset);
+  cudaError_t e = ingest_launch(q_src, src_dtype, b, d, src_row_stride, d_pad, cosine, qbuf, dev.sms, s,
+                                static_cast<uint32_t*>(workspace), round_up(p.clear_bytes, 4) / 4, p.qpad_rows);
+  if (e != cudaSuccess) return cuda_fail(e, "query ingest and workspace clear");
+  return launch_search(p, dev, qbuf, b, x_f16, n, d_pad, k, id_offset, out_scores, out_ids, workspace, s);
 }
 
 cvs_status cvs_scores(const void* q_f16, int64_t b, const void* x_f16, int64_t n, int d_pad,

@@ -259,9 +259,14 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
   return r;
 }
 
-// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope).
+// Arrive on an mbarrier of another CTA of the cluster. Release at CTA scope
+// only: the one use is "this CTA's drain warps have read the accumulator"
+// (their tcgen05.ld completed, tcgen05.wait::ld, before the arrive), an
+// execution order the partner's MMA thread needs, not the visibility of this
+// thread's memory writes at cluster scope -- waiting for those (the candidate
+// appends in flight to global memory) made every arrive cost a round trip.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
 

@@ -54,7 +54,7 @@ __device__ __forceinline__ bool tops_refresher(int q, int t, int list, int lists
 // costs a few hundred cycles against several thousand of MMA per tile), and the
 // first real tile needs every query's bound in place, so a refresher that runs
 // late on one CTA must not leave its query without one.
-constexpr int kDryRefreshers = 16;
+constexpr int kDryRefreshers = 6;
 
 // Shared per-query lower bound: the largest k-th-best score any list of this
 // query has reached (ordered bits, 0 = none yet). Every list of the query --
@@ -105,6 +105,40 @@ __device__ __forceinline__ float pick(const uint32_t (&r)[32], int j) {
 }
 
 constexpr int kTopsPerLane = 10;  // lists per query <= 320 for the in-kernel refresh
+
+// Raises the shared bound of every query in `need` (the lanes of this warp whose
+// query this list refreshes in this round) to the m-th largest value its lists
+// published (warp_kth_top). The whole warp serves one query at a time, and the
+// next query's published values are loaded while the current one is bisected,
+// so consecutive refreshes do not each wait a global-memory round trip.
+__device__ __forceinline__ void refresh_bounds(unsigned need, const uint32_t* tops, uint32_t* gthr, int q,
+                                               int lists, int m, float& bound, int lane) {
+  if (!need) return;
+  uint32_t cur[kTopsPerLane], nxt[kTopsPerLane];
+  int src = __ffs(need) - 1;
+  need &= need - 1;
+  int qs = __shfl_sync(kFullMask, q, src);
+  load_tops<kTopsPerLane>(tops + static_cast<size_t>(qs) * lists, lists, lane, cur);
+  while (true) {
+    int nsrc = -1, nqs = 0;
+    if (need) {
+      nsrc = __ffs(need) - 1;
+      need &= need - 1;
+      nqs = __shfl_sync(kFullMask, q, nsrc);
+      load_tops<kTopsPerLane>(tops + static_cast<size_t>(nqs) * lists, lists, lane, nxt);
+    }
+    const uint32_t kth = kth_of_tops<kTopsPerLane>(cur, m);
+    if (lane == src && kth != 0) {
+      atomicMax(gthr + qs, kth);
+      bound = fmaxf(bound, score_of_bits(kth));
+    }
+    if (nsrc < 0) break;
+    src = nsrc;
+    qs = nqs;
+#pragma unroll
+    for (int j = 0; j < kTopsPerLane; ++j) cur[j] = nxt[j];
+  }
+}
 
 // Dry tiles. A list starts empty, so without a shared bound its first tile
 // would send dozens of scores per query through the slow insertion path while

@@ -43,11 +43,31 @@ __device__ __forceinline__ __half load_as_half(const void* src, size_t i) {
   return __half();
 }
 
+// Work a search launch adds to its query ingest (cvs_search): zero `words`
+// 32-bit words at `p` (the workspace's bounds and counters) and write rows
+// n .. rows_pad-1 of the destination as zeros (the padding rows of the last
+// query tile), so that no separate preparation kernel is needed.
+struct IngestExtra {
+  uint32_t* p;
+  size_t words;
+  long long rows_pad;
+};
+
+__device__ __forceinline__ void ingest_extra(const IngestExtra& x, long long n, int d_pad, __half* dst) {
+  const size_t tid = static_cast<size_t>(blockIdx.x) * kIngestThreads + threadIdx.x;
+  const size_t nthreads = static_cast<size_t>(gridDim.x) * kIngestThreads;
+  for (size_t i = tid; i < x.words; i += nthreads) x.p[i] = 0u;
+  const size_t pad_chunks = static_cast<size_t>(x.rows_pad - n) * (d_pad / 8);  // 16-byte chunks
+  uint4* zdst = reinterpret_cast<uint4*>(dst + static_cast<size_t>(n) * d_pad);
+  for (size_t i = tid; i < pad_chunks; i += nthreads) zdst[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <int T>
 __global__ void __launch_bounds__(kIngestThreads) ingest_kernel(const void* src, long long n, int d,
                                                                 long long src_stride, int d_pad,
-                                                                int cosine, __half* dst) {
+                                                                int cosine, __half* dst, IngestExtra extra) {
   ingest_prologue();
+  ingest_extra(extra, n, d_pad, dst);
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (kIngestThreads / 32);
   for (long long row = static_cast<long long>(blockIdx.x) * (kIngestThreads / 32) + (threadIdx.x >> 5);
@@ -116,8 +136,9 @@ struct Chunk8 {
 template <int T, int CPL>
 __global__ void __launch_bounds__(kIngestThreads) ingest_vec_kernel(const void* src, long long n, int d,
                                                                     long long src_stride, int d_pad,
-                                                                    int cosine, __half* dst) {
+                                                                    int cosine, __half* dst, IngestExtra extra) {
   ingest_prologue();
+  ingest_extra(extra, n, d_pad, dst);
   const int lane = threadIdx.x & 31;
   const int dchunks = d >> 3, pchunks = d_pad >> 3;
   const long long warps = static_cast<long long>(gridDim.x) * (kIngestThreads / 32);
@@ -164,12 +185,12 @@ __global__ void __launch_bounds__(kIngestThreads) ingest_vec_kernel(const void* 
 
 template <int T>
 cudaError_t launch_vec(const void* src, long long n, int d, long long src_stride, int d_pad, int cosine,
-                       __half* dst, unsigned grid, cudaStream_t stream) {
+                       __half* dst, unsigned grid, const IngestExtra& extra, cudaStream_t stream) {
   const int cpl = (d_pad / 8 + 31) / 32;
 #define CVS_INGEST_VEC(C)                                                                          \
   if (cpl <= C) {                                                                                 \
     return launch_programmatic(ingest_vec_kernel<T, C>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, \
-                               src_stride, d_pad, cosine, dst);                                    \
+                               src_stride, d_pad, cosine, dst, extra);                             \
   }
   CVS_INGEST_VEC(1) CVS_INGEST_VEC(2) CVS_INGEST_VEC(3) CVS_INGEST_VEC(4) CVS_INGEST_VEC(6) CVS_INGEST_VEC(8)
 #undef CVS_INGEST_VEC
@@ -181,20 +202,26 @@ size_t elem_size(int t) { return t == kSrcF32 ? 4 : t == kSrcF64 ? 8 : 2; }
 }  // namespace
 
 cudaError_t ingest_launch(const void* src, int src_dtype, long long n, int d, long long src_stride,
-                          int d_pad, int cosine, __half* dst, int num_sms, cudaStream_t stream) {
+                          int d_pad, int cosine, __half* dst, int num_sms, cudaStream_t stream,
+                          uint32_t* clear, size_t clear_words, long long rows_pad) {
   if (n < 0 || d < 1 || d > 32 * kIngestMaxPerLane || d_pad < d) return cudaErrorInvalidValue;
-  if (n == 0) return cudaSuccess;
-  const long long want = (n + (kIngestThreads / 32) - 1) / (kIngestThreads / 32);
-  const unsigned grid = static_cast<unsigned>(std::min<long long>(want, static_cast<long long>(num_sms) * 8));
+  if (rows_pad < n) rows_pad = n;
+  if (n == 0 && rows_pad == 0 && clear_words == 0) return cudaSuccess;
+  const IngestExtra extra{clear, clear ? clear_words : 0, rows_pad};
+  // One warp per row; enough threads for the clear and the padding rows too.
+  const long long extra_work = static_cast<long long>(std::max<size_t>(extra.words, static_cast<size_t>(rows_pad - n) * (d_pad / 8)));
+  const long long want = std::max<long long>((n + (kIngestThreads / 32) - 1) / (kIngestThreads / 32),
+                                             (extra_work + kIngestThreads - 1) / kIngestThreads);
+  const unsigned grid = static_cast<unsigned>(std::max<long long>(1, std::min<long long>(want, static_cast<long long>(num_sms) * 8)));
   const size_t es = elem_size(src_dtype);
   const bool vec = d % 8 == 0 && d_pad <= 2048 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
                    (static_cast<size_t>(src_stride) * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
   if (vec) {
     switch (src_dtype) {
-      case kSrcF32: return launch_vec<kSrcF32>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
-      case kSrcF16: return launch_vec<kSrcF16>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
-      case kSrcBF16: return launch_vec<kSrcBF16>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
-      case kSrcF64: return launch_vec<kSrcF64>(src, n, d, src_stride, d_pad, cosine, dst, grid, stream);
+      case kSrcF32: return launch_vec<kSrcF32>(src, n, d, src_stride, d_pad, cosine, dst, grid, extra, stream);
+      case kSrcF16: return launch_vec<kSrcF16>(src, n, d, src_stride, d_pad, cosine, dst, grid, extra, stream);
+      case kSrcBF16: return launch_vec<kSrcBF16>(src, n, d, src_stride, d_pad, cosine, dst, grid, extra, stream);
+      case kSrcF64: return launch_vec<kSrcF64>(src, n, d, src_stride, d_pad, cosine, dst, grid, extra, stream);
       default: return cudaErrorInvalidValue;
     }
   }
@@ -202,19 +229,19 @@ cudaError_t ingest_launch(const void* src, int src_dtype, long long n, int d, lo
   switch (src_dtype) {
     case kSrcF32:
       e = launch_programmatic(ingest_kernel<kSrcF32>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
-                              d_pad, cosine, dst);
+                              d_pad, cosine, dst, extra);
       break;
     case kSrcF16:
       e = launch_programmatic(ingest_kernel<kSrcF16>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
-                              d_pad, cosine, dst);
+                              d_pad, cosine, dst, extra);
       break;
     case kSrcBF16:
       e = launch_programmatic(ingest_kernel<kSrcBF16>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
-                              d_pad, cosine, dst);
+                              d_pad, cosine, dst, extra);
       break;
     case kSrcF64:
       e = launch_programmatic(ingest_kernel<kSrcF64>, dim3(grid), dim3(kIngestThreads), 0, stream, src, n, d, src_stride,
-                              d_pad, cosine, dst);
+                              d_pad, cosine, dst, extra);
       break;
     default: return cudaErrorInvalidValue;
   }

@@ -183,7 +183,11 @@ cudaError_t merge_lists_launch(const MergeListsArgs& a, cudaStream_t stream);
 
 // ---- ingest: dtype conversion, optional L2 normalisation, width padding ----
 enum SrcDtype : int { kSrcF32 = 0, kSrcF16 = 1, kSrcBF16 = 2, kSrcF64 = 3 };
+// With `clear` given, the same launch also zeroes clear_words 32-bit words there,
+// and rows n .. rows_pad-1 of dst are written as zeros (a search's workspace
+// preparation folded into its query ingest).
 cudaError_t ingest_launch(const void* src, int src_dtype, long long n, int d, long long src_stride,
-                          int d_pad, int cosine, __half* dst, int num_sms, cudaStream_t stream);
+                          int d_pad, int cosine, __half* dst, int num_sms, cudaStream_t stream,
+                          uint32_t* clear = nullptr, size_t clear_words = 0, long long rows_pad = 0);
 
 }  // namespace cvs

@@ -134,32 +134,55 @@ __device__ __forceinline__ int warp_compact_ge(uint64_t* list, int m, uint64_t k
   return base;
 }
 
-// k-th largest of n published per-list maxima row[0..n) (ordered score bits,
-// 0 = none), computed by the whole warp: each lane loads up to PER_LANE of them
-// in one round trip, then a 32-step bisection on the value bits with warp-wide
-// counts finds the largest v such that at least k maxima are >= v. If k lists
-// hold a score >= v, at least k rows score >= v, so v bounds the query's k-th
-// best from below. Returns 0 when fewer than k lists have published.
-// Requires n <= 32 * PER_LANE.
+// A lower bound on the query's k-th best from n published per-list values
+// row[0..n) (ordered score bits, 0 = none), computed by the whole warp. If k
+// lists hold a score >= v, at least k rows score >= v, so any v with at least k
+// published values >= v bounds the query's k-th best from below; the best such
+// v is the k-th largest published value. Each lane loads up to PER_LANE values
+// in one round trip; a bisection on the ordered bits between the smallest and
+// the largest published value (the smallest qualifies: k or more values are at
+// or above it) then finds that value to within 2^-16 of the range -- stopping
+// early only returns a slightly lower, still valid, bound. Returns 0 when fewer
+// than k lists have published. Requires n <= 32 * PER_LANE.
 template <int PER_LANE>
-__device__ __forceinline__ uint32_t warp_kth_top(const uint32_t* row, int n, int k, int lane) {
-  uint32_t v[PER_LANE];
+__device__ __forceinline__ void load_tops(const uint32_t* row, int n, int lane, uint32_t (&v)[PER_LANE]) {
 #pragma unroll
   for (int j = 0; j < PER_LANE; ++j) {
     const int i = lane + 32 * j;
     v[j] = 0;
     if (i < n) asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v[j]) : "l"(row + i));
   }
-  uint32_t prefix = 0;
+}
+
+template <int PER_LANE>
+__device__ __forceinline__ uint32_t kth_of_tops(const uint32_t (&v)[PER_LANE], int k) {
+  uint32_t cnt = 0, mx = 0, mn = 0xFFFFFFFFu;
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    cnt += v[j] != 0 ? 1u : 0u;
+    mx = max(mx, v[j]);
+    mn = min(mn, v[j] != 0 ? v[j] : 0xFFFFFFFFu);
+  }
+  if (__reduce_add_sync(kFullMask, cnt) < static_cast<uint32_t>(k)) return 0;
+  uint32_t lo = __reduce_min_sync(kFullMask, mn);  // count(>= lo) >= k
+  uint32_t hi = __reduce_max_sync(kFullMask, mx);  // the answer is <= hi
 #pragma unroll 1
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t cand = prefix | (1u << bit);
+  for (int step = 0; step < 16 && lo < hi; ++step) {
+    const uint32_t mid = lo + (hi - lo + 1) / 2;
     uint32_t c = 0;
 #pragma unroll
-    for (int j = 0; j < PER_LANE; ++j) c += v[j] >= cand ? 1u : 0u;
-    if (__reduce_add_sync(kFullMask, c) >= static_cast<uint32_t>(k)) prefix = cand;
+    for (int j = 0; j < PER_LANE; ++j) c += v[j] >= mid ? 1u : 0u;
+    if (__reduce_add_sync(kFullMask, c) >= static_cast<uint32_t>(k)) lo = mid;
+    else hi = mid - 1;
   }
-  return prefix;
+  return lo;
+}
+
+template <int PER_LANE>
+__device__ __forceinline__ uint32_t warp_kth_top(const uint32_t* row, int n, int k, int lane) {
+  uint32_t v[PER_LANE];
+  load_tops<PER_LANE>(row, n, lane, v);
+  return kth_of_tops<PER_LANE>(v, k);
 }
 
 }  // namespace cvs

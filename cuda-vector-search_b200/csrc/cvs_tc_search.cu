@@ -328,18 +328,10 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         if (tops_round(t) && lists <= 32 * kTopsPerLane) {
           // This round's refresher of each query raises the query's shared bound
           // to the k-th largest published maximum; the whole warp serves each.
-          unsigned need = __ballot_sync(kFullMask, qvalid && tops_refresher(q, t, list, lists, dry ? kDryRefreshers : 1));
-          while (need) {
-            const int src = __ffs(need) - 1;
-            need &= need - 1;
-            const int qs = __shfl_sync(kFullMask, q, src);
-            const int mneed = (a.k + Epi::jrank(a.k, lists) - 1) / Epi::jrank(a.k, lists);
-            const uint32_t kth = warp_kth_top<kTopsPerLane>(a.tops + static_cast<size_t>(qs) * lists, lists, mneed, lane);
-            if (lane == src && kth != 0) {
-              atomicMax(a.gthr + qs, kth);
-              epi.bound = fmaxf(epi.bound, score_of_bits(kth));
-            }
-          }
+          const unsigned need =
+              __ballot_sync(kFullMask, qvalid && tops_refresher(q, t, list, lists, dry ? kDryRefreshers : 1));
+          const int mneed = (a.k + Epi::jrank(a.k, lists) - 1) / Epi::jrank(a.k, lists);
+          refresh_bounds(need, a.tops, a.gthr, q, lists, mneed, epi.bound, lane);
         }
       }
     }

@@ -112,6 +112,65 @@ std::vector<int64_t> fused_topk_into(torch::Tensor q, torch::Tensor x, int64_t k
   return {plan[0], plan[1]};
 }
 
+void check_raw_queries(const torch::Tensor& q, const torch::Tensor& x) {
+  TORCH_CHECK(q.is_cuda(), "queries must be a CUDA tensor");
+  TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1, "queries must be 2-D with contiguous rows");
+  TORCH_CHECK(q.device() == x.device(), "queries and corpus must be on the same device");
+  TORCH_CHECK(q.size(1) <= x.size(1), "queries are wider than the corpus");
+}
+
+int src_code(const torch::Tensor& t);
+
+// Search from raw queries (any supported float dtype, not yet normalised or
+// padded): [scores f32 [b,k], ids i64 [b,k]].
+std::vector<torch::Tensor> search(torch::Tensor q, torch::Tensor x, int64_t k, bool cosine) {
+  check_matrix(x, "corpus");
+  check_raw_queries(q, x);
+  TORCH_CHECK(k >= 1 && k <= CVS_MAX_FUSED_K, "search supports 1 <= k <= ", CVS_MAX_FUSED_K);
+  TORCH_CHECK(k <= x.size(0), "k must not exceed the corpus size");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int64_t b = q.size(0), n = x.size(0);
+  const int d_pad = static_cast<int>(x.size(1));
+  auto out_v = torch::empty({b, k}, x.options().dtype(torch::kFloat));
+  auto out_i = torch::empty({b, k}, x.options().dtype(torch::kLong));
+  if (b == 0) return {out_v, out_i};
+  size_t ws_bytes = 0;
+  check(cvs_search_workspace_size(b, n, d_pad, static_cast<int>(k), &ws_bytes), "search");
+  auto ws = torch::empty({static_cast<int64_t>(std::max<size_t>(ws_bytes, 256))}, x.options().dtype(torch::kUInt8));
+  check(cvs_search(q.data_ptr(), src_code(q), b, static_cast<int>(q.size(1)), q.stride(0), cosine ? 1 : 0,
+                   x.data_ptr(), n, d_pad, static_cast<int>(k), 0, out_v.data_ptr<float>(), out_i.data_ptr<int64_t>(),
+                   ws.data_ptr(), static_cast<size_t>(ws.numel()), stream_of(x)),
+        "search");
+  return {out_v, out_i};
+}
+
+// The same into caller-provided outputs and workspace, with a global id offset
+// (row-sharded corpora).
+void search_into(torch::Tensor q, torch::Tensor x, int64_t k, bool cosine, int64_t id_offset, torch::Tensor out_v,
+                 torch::Tensor out_i, torch::Tensor ws) {
+  check_matrix(x, "corpus");
+  check_raw_queries(q, x);
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(out_v.is_cuda() && out_v.scalar_type() == torch::kFloat && out_v.is_contiguous() &&
+                  out_v.numel() == q.size(0) * k,
+              "out_v must be a contiguous float32 CUDA tensor of b*k elements");
+  TORCH_CHECK(out_i.is_cuda() && out_i.scalar_type() == torch::kLong && out_i.is_contiguous() &&
+                  out_i.numel() == q.size(0) * k,
+              "out_i must be a contiguous int64 CUDA tensor of b*k elements");
+  TORCH_CHECK(ws.is_cuda() && ws.is_contiguous(), "workspace must be a contiguous CUDA tensor");
+  check(cvs_search(q.data_ptr(), src_code(q), q.size(0), static_cast<int>(q.size(1)), q.stride(0), cosine ? 1 : 0,
+                   x.data_ptr(), x.size(0), static_cast<int>(x.size(1)), static_cast<int>(k), id_offset,
+                   out_v.data_ptr<float>(), out_i.data_ptr<int64_t>(), ws.data_ptr(),
+                   static_cast<size_t>(ws.numel() * ws.element_size()), stream_of(x)),
+        "search");
+}
+
+int64_t search_workspace_size(int64_t b, int64_t n, int64_t d_pad, int64_t k) {
+  size_t bytes = 0;
+  check(cvs_search_workspace_size(b, n, static_cast<int>(d_pad), static_cast<int>(k), &bytes), "search_workspace_size");
+  return static_cast<int64_t>(bytes);
+}
+
 int64_t workspace_size(int64_t b, int64_t n, int64_t d_pad, int64_t k, int64_t chunks) {
   size_t bytes = 0;
   check(cvs_fused_topk_workspace_size(b, n, static_cast<int>(d_pad), static_cast<int>(k), 0,
@@ -191,6 +250,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_topk_into", &fused_topk_into, "Fused top-k into given outputs with an id offset",
         py::arg("q"), py::arg("x"), py::arg("k"), py::arg("id_offset"), py::arg("out_v"),
         py::arg("out_i"), py::arg("workspace"), py::arg("chunks") = 0);
+  m.def("search", &search, "Search from raw queries (prepared in the search's first launch)", py::arg("q"),
+        py::arg("x"), py::arg("k"), py::arg("cosine"));
+  m.def("search_into", &search_into, "search() into given outputs and workspace, with an id offset", py::arg("q"),
+        py::arg("x"), py::arg("k"), py::arg("cosine"), py::arg("id_offset"), py::arg("out_v"), py::arg("out_i"),
+        py::arg("ws"));
+  m.def("search_workspace_size", &search_workspace_size, "Workspace bytes for search_into", py::arg("b"),
+        py::arg("n"), py::arg("d_pad"), py::arg("k"));
   m.def("workspace_size", &workspace_size, "Workspace bytes for fused_topk_into", py::arg("b"),
         py::arg("n"), py::arg("d_pad"), py::arg("k"), py::arg("chunks") = 0);
   m.def("ingest_into", &ingest_into, "Convert / normalise / pad rows into an fp16 matrix",

@@ -7,12 +7,13 @@ underneath:
 
 * storage: one ingest kernel converts to fp16, L2-normalises (cosine) and pads
   the width to a multiple of 64 in a single pass (index.py:35-41 + 27-32 there);
-* search: ``method="fused"`` (the default) runs the tcgen05 score + top-k kernel
-  (or the GEMV kernel for a single query) and a merge kernel; queries in
-  pinned host memory are copied on a side stream, so a caller that issues the
-  next search before reading back the previous results overlaps each upload
-  with the previous search (a fixed ring of device buffers, nothing allocated
-  per call);
+* search: ``method="fused"`` (the default) is three launches: the queries'
+  preparation (to fp16, normalised for cosine, padded) fused with the
+  workspace clear, the tcgen05 score + top-k kernel (or the GEMV kernel for a
+  single query), and a merge kernel; queries in pinned host memory are copied
+  on a side stream, so a caller that issues the next search before reading
+  back the previous results overlaps each upload with the previous search (a
+  fixed ring of device buffers, nothing allocated per call);
 * there is no CPU storage and no fallback: a non-CUDA device or a GPU other than
   sm_100 raises RuntimeError. ``method="torch"`` (cuBLAS + topk) remains available
   on request, as in the reference.
@@ -64,8 +65,11 @@ class _UploadRing:
         self.next = 0
         self.lock = threading.Lock()
 
-    def ingest(self, blk: torch.Tensor, out: torch.Tensor, cosine: bool, mod) -> None:
-        """Upload pinned ``blk`` and run the ingest kernel from it into ``out``."""
+    def upload(self, blk: torch.Tensor):
+        """Copy pinned ``blk`` into the next slot on the side stream; the current
+        stream waits for the copy. Returns the device copy and a callable to run
+        once the kernels that read it are enqueued (it marks the slot reusable
+        after them)."""
         cur = torch.cuda.current_stream(self.device)
         nelem = blk.numel()
         with self.lock:
@@ -84,12 +88,25 @@ class _UploadRing:
             with torch.cuda.stream(self.side):
                 dst.copy_(blk, non_blocking=True)
             cur.wait_stream(self.side)
-            mod.ingest_into(dst, out, cosine)
-            self.consumed[j].record(cur)
             self.used[j] = True
+
+        def release():
+            self.consumed[j].record(cur)
+
+        return dst, release
+
+    def ingest(self, blk: torch.Tensor, out: torch.Tensor, cosine: bool, mod) -> None:
+        """Upload pinned ``blk`` and run the ingest kernel from it into ``out``."""
+        dst, release = self.upload(blk)
+        mod.ingest_into(dst, out, cosine)
+        release()
 
 
 _RINGS: dict = {}  # device index -> _UploadRing
+
+
+def _nothing() -> None:
+    pass
 
 
 def _upload_ring(device: torch.device) -> _UploadRing:
@@ -204,6 +221,26 @@ class Index:
         """The stored matrix (normalised for cosine), without padding."""
         return self._x[:, : self.dim]
 
+    def _device_queries(self, queries):
+        """Raw queries as a 2-D tensor on the index device with contiguous rows,
+        not yet converted, normalised or padded (the search's first launch does
+        that), and a callable to run once the search is enqueued. Pinned host
+        queries of 256 KB and more are copied on the upload ring's side stream."""
+        q = _to_tensor(queries)
+        if q.dim() == 1:
+            q = q[None]
+        if q.dim() != 2 or q.shape[1] != self.dim:
+            raise ValueError(f"queries must be [b, {self.dim}]")
+        if q.dtype not in _KERNEL_DTYPES:
+            q = q.to(torch.float32)
+        if q.device == self.device:
+            return (q if q.stride(1) == 1 else q.contiguous()), _nothing
+        if q.is_pinned() and q.is_contiguous() and _SIDE_UPLOAD_BYTES <= q.nbytes <= _RING_MAX_BYTES:
+            with torch.cuda.device(self.device):
+                return _upload_ring(self.device).upload(q)
+        q = q.to(self.device, non_blocking=q.is_pinned())
+        return (q if q.stride(1) == 1 else q.contiguous()), _nothing
+
     def _prep_queries(self, queries) -> torch.Tensor:
         q = _to_tensor(queries)
         if q.dim() == 1:
@@ -228,15 +265,18 @@ class Index:
         if k < 1:
             raise ValueError("k must be >= 1")
         k = min(k, len(self))
-        q = self._prep_queries(queries)
         if method == "auto":
             method = "fused" if k <= MAX_FUSED_K else "twopass"
         mod = _ext.load()
         if method == "fused":
+            q, release = self._device_queries(queries)
             if k > MAX_FUSED_K:
                 raise ValueError(f"fused search supports k <= {MAX_FUSED_K}")
-            v, i, _ = mod.fused_topk(q, self._x, k)
+            # Query preparation, workspace clear, search and merge: three launches.
+            v, i = mod.search(q, self._x, k, self.metric == "cosine")
+            release()
             return v, i
+        q = self._prep_queries(queries)
         if method == "twopass":
             s = mod.scores(q, self._x, False)
             v, i = torch.topk(s, k, dim=1)

@@ -85,32 +85,35 @@ def cuda_shard_ops(index: Index) -> ShardOps:
     mod = _ext.load()
     workspaces: dict = {}
 
+    cosine = index.metric == "cosine"
+
     def workspace(b, kk):
         ws = workspaces.get((b, kk))
         if ws is None:
-            ws = torch.empty(max(256, mod.workspace_size(b, len(index), index._x.shape[1], kk)),
+            ws = torch.empty(max(256, mod.search_workspace_size(b, len(index), index._x.shape[1], kk)),
                              dtype=torch.uint8, device=index.device)
             workspaces[(b, kk)] = ws
         return ws
 
     def local_topk_into(queries, k, id_offset, v, i):
-        q = index._prep_queries(queries)
+        q, release = index._device_queries(queries)
         b = q.shape[0]
         kk = min(k, len(index))
         ws = workspace(b, kk)
         if kk == k:
-            mod.fused_topk_into(q, index._x, kk, id_offset, v, i, ws)
+            mod.search_into(q, index._x, kk, cosine, id_offset, v, i, ws)
         else:  # shard smaller than k: its kk results, then empty slots
             vk = torch.empty((b, kk), dtype=torch.float32, device=index.device)
             ik = torch.empty((b, kk), dtype=torch.int64, device=index.device)
-            mod.fused_topk_into(q, index._x, kk, id_offset, vk, ik, ws)
+            mod.search_into(q, index._x, kk, cosine, id_offset, vk, ik, ws)
             v[:, :kk] = vk
             i[:, :kk] = ik
             v[:, kk:] = float("-inf")
             i[:, kk:] = -1
+        release()
 
     def local_topk(queries, k, id_offset):
-        b = index._prep_queries(queries).shape[0]
+        b = 1 if getattr(queries, "ndim", 2) == 1 else len(queries)
         v = torch.empty((b, k), dtype=torch.float32, device=index.device)
         i = torch.empty((b, k), dtype=torch.int64, device=index.device)
         local_topk_into(queries, k, id_offset, v, i)

@@ -89,6 +89,30 @@ cvs_status cvs_fused_topk(const void* q_f16, int64_t b, const void* x_f16, int64
                           int64_t* plan_out, void* stream);
 
 /*
+ * Bytes of device workspace cvs_search needs (automatic plan): the candidate
+ * lists and bounds of cvs_fused_topk plus the prepared queries, padded to
+ * whole query tiles.
+ */
+cvs_status cvs_search_workspace_size(int64_t b, int64_t n, int d_pad, int k, size_t* bytes);
+
+/*
+ * Exact top-k search straight from raw queries, as Index.search does it: the
+ * queries' preparation (cvs_ingest's arithmetic: to fp16, L2 normalisation when
+ * cosine != 0, zero padding to d_pad) runs in the same launch that clears the
+ * workspace, and writes the prepared queries into the workspace, so a search
+ * is three launches (prepare, search, merge) and the caller keeps no
+ * prepared-query buffer. Results as for cvs_fused_topk with the automatic plan.
+ *   q_src: [b][d] rows src_row_stride elements apart, dtype src_dtype, in
+ *   device memory or host memory the device can address; d <= d_pad.
+ *   workspace: at least cvs_search_workspace_size() bytes, 256-byte aligned.
+ * Replaces: Index._prep_queries + fused_topk as called by Index.search
+ * (cuda_vector_search/index.py:89-98, 118-125).
+ */
+cvs_status cvs_search(const void* q_src, int src_dtype, int64_t b, int d, int64_t src_row_stride, int cosine,
+                      const void* x_f16, int64_t n, int d_pad, int k, int64_t id_offset, float* out_scores,
+                      int64_t* out_ids, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Full score matrix out[b][n] = q . x^T, fp32 (out_fp32 != 0) or fp16.
  * Replaces: scores (cuda_vector_search/csrc/kernels.cu:472-497, bound at
  * :588-589; kernel score_kernel :285-311).
