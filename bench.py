@@ -533,17 +533,22 @@ def run_ours(args, cfg):
 
     # Untimed afterwards: where a sharded step's time goes (CUDA events on the
     # current stream around the local search, the all-gather and the merge).
+    # Steps run back to back as in the timed loop (no host synchronisation
+    # between them, which would turn host-side skew between the ranks into
+    # all-gather time); each step records its own four events.
     phases = [0.0, 0.0, 0.0]
     if world > 1:
-        pev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        index.phase_events = pev
         reps = min(args.steps, 20)
-        for _ in range(reps):
+        pevs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(reps)]
+        barrier()
+        for pev in pevs:
+            index.phase_events = pev
             step(q_dev)
-            pev[3].synchronize()
+        index.phase_events = None
+        torch.cuda.synchronize()
+        for pev in pevs:
             for j in range(3):
                 phases[j] += pev[j].elapsed_time(pev[j + 1]) * 1e3 / reps
-        index.phase_events = None
     tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)] + phases, dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -605,7 +610,7 @@ def run_ours(args, cfg):
         if world > 1:
             out["phases_us"] = {"local_search": round(phases[0], 1), "all_gather": round(phases[1], 1),
                                 "merge": round(phases[2], 1),
-                                "note": "max over ranks of the mean of up to 20 untimed steps after the timed loops"}
+                                "note": "max over ranks of the mean of up to 20 untimed back-to-back steps after the timed loops; all_gather includes waiting for the slowest rank's local search"}
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(cfg)
         print(json.dumps(out), flush=True)

@@ -81,3 +81,27 @@ def test_merge_and_ingest_contracts(lib):
     assert lib.cvs_ingest(16, 0, 5, 100, 100, 96, 1, 16, None) == 1  # d_pad not a multiple of 64
     assert lib.cvs_ingest(16, 9, 5, 64, 64, 64, 1, 32, None) == 1  # unknown dtype
     assert b"dtype" in lib.cvs_last_error()
+
+
+def test_search_contract_errors_before_any_device_use(lib):
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    f = lib.cvs_search
+    f.argtypes = [vp, i32, i64, i32, i64, i32, vp, i64, i32, i32, i64, vp, vp, vp, ctypes.c_size_t, vp]
+    assert f(None, 0, 4, 64, 64, 1, 16, 100, 64, 10, 0, 16, 16, 256, 1 << 20, None) == 1
+    assert b"queries" in lib.cvs_last_error()
+    assert f(16, 0, 4, 100, 100, 1, 16, 100, 64, 10, 0, 16, 16, 256, 1 << 20, None) == 1  # wider than the corpus
+    assert b"exceeds" in lib.cvs_last_error()
+    assert f(16, 7, 4, 64, 64, 1, 16, 100, 64, 10, 0, 16, 16, 256, 1 << 20, None) == 1  # unknown dtype
+    assert f(16, 0, 4, 64, 32, 1, 16, 100, 64, 10, 0, 16, 16, 256, 1 << 20, None) == 1  # stride < width
+    assert f(16, 0, 0, 64, 64, 1, 16, 100, 64, 10, 0, 16, 16, 256, 1 << 20, None) == 0  # no queries: nothing to do
+    n = ctypes.c_size_t(0)
+    g = lib.cvs_search_workspace_size
+    g.argtypes = [i64, i64, i32, i32, ctypes.POINTER(ctypes.c_size_t)]
+    assert g(4, 1000, 100, 10, ctypes.byref(n)) == 1
+    assert g(0, 10, 128, 10, ctypes.byref(n)) == 0 and n.value == 0
+
+
+def test_stall_hook_rejects_out_of_range_limits(lib):
+    lib.cvs_debug_stall_next_search.argtypes = [ctypes.c_int64]
+    assert lib.cvs_debug_stall_next_search(10) == 1
+    assert lib.cvs_debug_stall_next_search(1 << 50) == 1
