@@ -531,6 +531,24 @@ def run_ours(args, cfg):
     clk = clocks.stop(windows=[(host_t0, host_t1), (host_e0, host_t2)])
     e2e_ms_total = e2e_flushed_ms if flush_buf is not None else e2e_t0.elapsed_time(e2e_t1)
 
+    # Untimed afterwards: the same K steps without the profiling events. The
+    # events sit between the kernels of a search and break their programmatic-
+    # launch chain (measured: +10 us per C1 call, +1% at C2), so the timed loop
+    # above, which carries them for the roofline, slightly overstates the step.
+    barrier()
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    u0.record(stream)
+    for s in range(args.steps):
+        if flush_buf is not None:
+            flush(s)
+            step_evs[s][0].record(stream)
+        step(q_dev)
+        if flush_buf is not None:
+            step_evs[s][1].record(stream)
+    u1.record(stream)
+    barrier()
+    plain_ms_total = sum(a.elapsed_time(bb) for a, bb in step_evs) if flush_buf is not None else u0.elapsed_time(u1)
+
     # Untimed afterwards: where a sharded step's time goes (CUDA events on the
     # current stream around the local search, the all-gather and the merge).
     # Steps run back to back as in the timed loop (no host synchronisation
@@ -549,11 +567,12 @@ def run_ours(args, cfg):
         for pev in pevs:
             for j in range(3):
                 phases[j] += pev[j].elapsed_time(pev[j + 1]) * 1e3 / reps
-    tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms)] + phases, dtype=torch.float64, device=dev)
+    tt = torch.tensor([ms_total, e2e_ms_total, sum(kern_ms), plain_ms_total] + phases, dtype=torch.float64,
+                      device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms_total, e2e_ms_total, kern_total = tt.tolist()[:3]
-    phases = tt.tolist()[3:]
+    ms_total, e2e_ms_total, kern_total, plain_ms_total = tt.tolist()[:4]
+    phases = tt.tolist()[4:]
     parity = None if args.no_parity else parity_check(torch, local_index, q_dev, step(q_dev), k,
                                                        index.row_offset if world > 1 else 0, world)
     ms = ms_total / args.steps
@@ -579,9 +598,9 @@ def run_ours(args, cfg):
                     "frac": round(gbs / hbm_peak, 4), "traffic": traffic,
                     "note": f"copy bandwidth, {peak_src}; algorithmic bytes = corpus + queries + results"}
         roofline = roof_tc if bound == "tensor" else roof_hbm
-        # Our kernels per step: query ingest, workspace prepare, search, merge of
-        # the segment lists (+ the merge of the gathered shard lists).
-        launches_per_step = 4 if world == 1 else 5
+        # Our kernels per step: query preparation fused with the workspace clear,
+        # search, merge of the segment lists (+ the merge of the gathered shard lists).
+        launches_per_step = 3 if world == 1 else 4
         out = {
             "metric": METRIC,
             "value": round(value, 1),
@@ -606,6 +625,12 @@ def run_ours(args, cfg):
             "clocks": clk,
             "gpu_launches": launches_per_step * args.steps,
             "parity": parity,
+            "without_kernel_events": {
+                "ms_per_step": round(plain_ms_total / args.steps, 4),
+                "value": round(world * b / (plain_ms_total / args.steps / 1e3), 1),
+                "note": ("the same K steps after the timed loop without the per-step profiling events that time "
+                         "the search kernel (they break the launch chain between its kernels); untimed, max over ranks"),
+            },
         }
         if world > 1:
             out["phases_us"] = {"local_search": round(phases[0], 1), "all_gather": round(phases[1], 1),
@@ -687,6 +712,25 @@ def run_sweep(args, cfg):
         Path(args.report).write_text(table + "\n")
 
 
+def run_merge_case(args):
+    """Profiling case for the multi-GPU merge kernel on one GPU: merge_lists over
+    gathered [ranks, b, k] lists of the C5 8-GPU shape (8 x 1024 x 100), five
+    calls (no timing, no JSON line)."""
+    import torch
+
+    from cuda_vector_search import _ext
+
+    mod = _ext.load()
+    ranks, b, k = 8, 1024, 100
+    g = torch.Generator(device="cuda").manual_seed(3)
+    v = torch.rand(ranks, b, k, device="cuda", generator=g).sort(dim=2, descending=True).values.contiguous()
+    i = torch.randint(0, 1 << 30, (ranks, b, k), device="cuda", generator=g)
+    for _ in range(5):
+        mod.merge_lists(v, i, k)
+    torch.cuda.synchronize()
+    print("merge_lists case done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -705,13 +749,17 @@ def main():
     ap.add_argument("--sweep-batches", default="1,2,8,32,128,256,512,1024")
     ap.add_argument("--sweep-chunks", default="0")
     ap.add_argument("--report", default="", help="with --sweep: write the markdown table to this path")
+    ap.add_argument("--merge-case", action="store_true",
+                    help="profiling case: merge_lists over [8, 1024, 100] gathered lists (one GPU)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.rows:
         cfg["n"] = args.rows
     if args.batch:
         cfg["b"] = args.batch
-    if args.sweep:
+    if args.merge_case:
+        run_merge_case(args)
+    elif args.sweep:
         run_sweep(args, cfg)
     elif args.impl == "reference":
         run_reference(args, cfg)
