@@ -37,10 +37,14 @@ __device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
 }
 
 // Rounds at which a query's bound is recomputed from the lists' published
-// values: after tiles 0..7, then after every fourth tile. In each round one
-// list per query (a rotating choice, spreading the work over the CTAs) does it,
-// kDryRefreshers lists in dry rounds.
-__device__ __forceinline__ bool tops_round(int t) { return t < 8 || (t & 3) == 3; }
+// values: after tiles 0..7, then after every 16th tile. In each round one list
+// per query (a rotating choice, spreading the work over the CTAs) does it,
+// kDryRefreshers lists in dry rounds. Later refreshes tighten an already close
+// bound little, and each one delays its warp's next drain -- with 16 drain
+// warps per CTA pair behind one accumulator barrier, a slow warp stalls the
+// MMA: every 16th tile instead of every 4th measured -5% at 4M x 768, b=1024,
+// k=100 and -4% at C4 k=100, neutral elsewhere.
+__device__ __forceinline__ bool tops_round(int t) { return t < 8 || (t & 15) == 15; }
 
 // The r lists h, h+1, ..., h+r-1 (mod lists) refresh query q in round t.
 __device__ __forceinline__ bool tops_refresher(int q, int t, int list, int lists, int r) {
