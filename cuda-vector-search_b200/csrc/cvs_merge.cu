@@ -28,9 +28,15 @@ constexpr int kKeysWarps = kKeysThreads / 32;
 constexpr int kKeysBatch = 8;         // keys in flight per lane
 constexpr int kMergeTopsPerLane = 32;  // up to 1024 lists per query
 
-// Shared memory per warp of the list merge: radix histogram, k selected keys.
+// Keys of one query staged in shared memory by the list merge (one 64-bit key
+// per (score, id) pair), so that the radix passes re-read shared memory instead
+// of global memory: up to 2048 keys, e.g. 8 ranks x k = 256.
+constexpr int kMergeStageKeys = 2048;
+
+// Shared memory per warp of the list merge: radix histogram, k selected keys,
+// staged keys.
 __host__ __device__ constexpr size_t merge_warp_bytes(int k) {
-  return 256 * 4 + static_cast<size_t>(k) * 8;
+  return 256 * 4 + static_cast<size_t>(k) * 8 + static_cast<size_t>(kMergeStageKeys) * 8;
 }
 
 // Survivors of the bound filter kept in shared memory (4k, at least 512).
@@ -332,8 +338,31 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const Mer
   uint64_t* sel = reinterpret_cast<uint64_t*>(mine + 256 * 4);
   if (q >= a.b) return;
   const ListKeys acc{a.v, a.ids, a.v_stride, a.i_stride, a.len, q};
-  select_and_emit(acc, a.lists * a.len, a.k, 0, hist, sel, a.out_v + static_cast<size_t>(q) * a.k,
-                  a.out_i + static_cast<size_t>(q) * a.k, lane);
+  const int m = a.lists * a.len;
+  float* out_v = a.out_v + static_cast<size_t>(q) * a.k;
+  long long* out_i = a.out_i + static_cast<size_t>(q) * a.k;
+  if (m <= kMergeStageKeys) {
+    // Each (score, id) pair is read from global memory once, four pairs in
+    // flight per lane, and becomes a key in shared memory for the selection.
+    uint64_t* stage = sel + a.k;
+    for (int i0 = 0; i0 < m; i0 += 128) {
+      uint64_t key[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + 32 * u + lane;
+        key[u] = i < m ? acc(i) : 0ull;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + 32 * u + lane;
+        if (i < m) stage[i] = key[u];
+      }
+    }
+    __syncwarp();
+    select_and_emit(ContigKeys{stage}, m, a.k, 0, hist, sel, out_v, out_i, lane);
+    return;
+  }
+  select_and_emit(acc, m, a.k, 0, hist, sel, out_v, out_i, lane);
 }
 
 size_t merge_smem(int k) { return kMergeWarps * merge_warp_bytes(k); }

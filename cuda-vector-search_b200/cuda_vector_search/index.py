@@ -226,11 +226,7 @@ class Index:
         not yet converted, normalised or padded (the search's first launch does
         that), and a callable to run once the search is enqueued. Pinned host
         queries of 256 KB and more are copied on the upload ring's side stream."""
-        q = _to_tensor(queries)
-        if q.dim() == 1:
-            q = q[None]
-        if q.dim() != 2 or q.shape[1] != self.dim:
-            raise ValueError(f"queries must be [b, {self.dim}]")
+        q = self._query_tensor(queries)
         if q.dtype not in _KERNEL_DTYPES:
             q = q.to(torch.float32)
         if q.device == self.device:
@@ -241,13 +237,17 @@ class Index:
         q = q.to(self.device, non_blocking=q.is_pinned())
         return (q if q.stride(1) == 1 else q.contiguous()), _nothing
 
-    def _prep_queries(self, queries) -> torch.Tensor:
+    def _query_tensor(self, queries) -> torch.Tensor:
+        """The queries as a 2-D tensor, validated like the reference (index.py:89-94)."""
         q = _to_tensor(queries)
         if q.dim() == 1:
             q = q[None]
         if q.dim() != 2 or q.shape[1] != self.dim:
             raise ValueError(f"queries must be [b, {self.dim}]")
-        return _ingest(q, self.device, self.metric == "cosine")
+        return q
+
+    def _prep_queries(self, queries) -> torch.Tensor:
+        return _ingest(self._query_tensor(queries), self.device, self.metric == "cosine")
 
     # -- search -------------------------------------------------------------
     def search(self, queries, k: int = 10, method: str = "auto"):
@@ -269,9 +269,10 @@ class Index:
             method = "fused" if k <= MAX_FUSED_K else "twopass"
         mod = _ext.load()
         if method == "fused":
-            q, release = self._device_queries(queries)
             if k > MAX_FUSED_K:
+                self._query_tensor(queries)  # the reference reports bad queries first
                 raise ValueError(f"fused search supports k <= {MAX_FUSED_K}")
+            q, release = self._device_queries(queries)
             # Query preparation, workspace clear, search and merge: three launches.
             v, i = mod.search(q, self._x, k, self.metric == "cosine")
             release()

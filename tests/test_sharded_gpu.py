@@ -122,3 +122,31 @@ def test_save_then_load_whole_and_per_shard_ranges(mod, tmp_path):
         ids.append(pi)
     mv, mi = mod.merge_lists(torch.stack(vs).contiguous(), torch.stack(ids).contiguous(), k)
     assert_topk_exact(mv.cpu().numpy(), mi.cpu().numpy(), q32, x32, ov, oi, k)
+
+
+@pytest.mark.parametrize("lists,b,length,k", [(8, 256, 10, 10), (8, 300, 100, 100), (5, 64, 256, 200),
+                                              (3, 40, 1024, 1024), (2, 7, 17, 5)])
+def test_merge_lists_matches_the_oracle_merge(mod, lists, b, length, k):
+    """merge_lists (the merge after the all-gather) against oracle.merge_topk,
+    with exact score ties across lists and empty slots (id -1) in short shards;
+    the first four shapes take the shared-memory staged path, (3, 40, 1024)
+    the global-memory one."""
+    import numpy as np
+
+    from oracle import merge_topk
+
+    g = torch.Generator().manual_seed(lists * 1000 + length)
+    v = torch.randn(lists, b, length, generator=g).round(decimals=2)  # many exact ties
+    ids = torch.stack([torch.stack([torch.randperm(1 << 20, generator=g)[:length] + (l << 20) for _ in range(b)])
+                       for l in range(lists)])
+    v, order = v.sort(dim=2, descending=True)
+    ids = ids.gather(2, order)
+    ids[0, :, length - 3:] = -1  # a shard with fewer rows than k: empty slots
+    v[0, :, length - 3:] = float("-inf")
+    mv, mi = mod.merge_lists(v.cuda().contiguous(), ids.cuda().contiguous(), k)
+    vs = [np.where(ids[l].numpy() >= 0, v[l].numpy(), -np.inf).astype(np.float32) for l in range(lists)]
+    js = [np.where(ids[l].numpy() >= 0, ids[l].numpy(), np.iinfo(np.int64).max) for l in range(lists)]
+    rv, ri = merge_topk(vs, js, k)
+    ri = np.where(ri == np.iinfo(np.int64).max, -1, ri)
+    assert np.array_equal(mi.cpu().numpy(), ri)
+    assert np.array_equal(mv.cpu().numpy(), rv)
