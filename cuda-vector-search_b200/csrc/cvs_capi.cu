@@ -231,10 +231,11 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     p->cap = k;
   } else {
     p->epi = kEpiTopkBuf;
-    // Room for 2k keys, and at least for the first two tiles' 256 columns of a
-    // list (appended before any shared bound exists) plus one chunk, so that
-    // no list compacts in its first two tiles.
-    p->cap = static_cast<int>(round_up(static_cast<size_t>(std::max({2 * k, k + 32, 2 * kTcN / 2 + 64})), 32));
+    // Room for 2k keys and at least 256 (the shared-memory compaction buffer),
+    // and always a chunk (32 keys) above k. Lists start appending with a bound
+    // in place (dry tiles), so they rarely compact: none at all in the C4 and
+    // b = 1024, k = 100 shapes.
+    p->cap = static_cast<int>(round_up(static_cast<size_t>(std::max({2 * k, k + 32, 256})), 32));
   }
   plan_tc_grid(p, b, n, dev.sms, chunks, p->epi, d_pad, bq);
   p->lists = p->segs * tc_lists_per_segment(p->epi);

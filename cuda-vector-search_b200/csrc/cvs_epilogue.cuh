@@ -278,7 +278,7 @@ struct EpiTopkBuf {
   // Two column stripes per TMEM quadrant, as the register lists.
   static constexpr int kSubs = 2;
   static constexpr bool kTops = true;
-  static constexpr int kScratchKeys = 512;  // shared-memory compaction up to cap 512 (k <= 256)
+  static constexpr int kScratchKeys = 256;  // shared-memory compaction up to 256 keys (cap 256: k <= 112)
   static constexpr int kRegJ = RJ;  // J-th best tracked in registers for J <= kRegJ
   static __device__ __forceinline__ int jrank(int k, int lists) { return tops_j(k, lists, RJ); }
   uint64_t* list;

@@ -15,7 +15,12 @@ namespace cvs {
 constexpr int kTcM = 128;          // queries per tile (MMA M; TMEM lanes)
 constexpr int kTcN = 256;          // corpus rows per tile (MMA N; TMEM columns)
 constexpr int kTcK = 64;           // halves per K slice (one 128-byte swizzled row)
-constexpr int kTcStages = 4;
+// Ring stages of the tcgen05 kernels: as many as the shared memory left after
+// the resident queries, barriers, iteration log and (buffer epilogues) radix
+// histograms and compaction buffers holds, at most this many (the barrier
+// arrays are sized for it).
+constexpr int kTcMaxStages = 8;
+constexpr int kSmemBudget = 232448 - 1024;  // dynamic shared memory per CTA, less the alignment slack
 constexpr int kTcMaxResidentSlices = 7;  // queries stay in smem when d_pad <= 448
 // Dry tiles of the top-k epilogues (see cvs_epilogue.cuh): at most this many
 // (TileSource in cvs_sched.cuh keeps two).

@@ -38,17 +38,20 @@ namespace {
 constexpr int kRows = kTcN / 2;                  // corpus rows per CTA per tile
 constexpr int kQSlice = kTcM * kTcK * 2;         // 16 KB: 128 queries x 64 halves
 constexpr int kXHalf = kRows * kTcK * 2;         // 16 KB: 128 corpus rows x 64 halves
-constexpr int kStages = 6;  // barrier arrays are sized for this many stages
-// Ring depth: 6 stages, or 5 when the epilogue needs shared-memory compaction
-// buffers (8 warps x 4 KB).
-__host__ __device__ constexpr int pair_stages(int scratch_keys) { return scratch_keys > 0 ? 5 : kStages; }
+constexpr int kStages = kTcMaxStages;  // barrier arrays are sized for this many stages
 constexpr uint32_t kTmemCols = 512;
 
 __host__ __device__ constexpr int pair_epi_warps(int subs) { return 4 * subs; }
 __host__ __device__ constexpr int pair_threads(int subs) { return 64 + 32 * pair_epi_warps(subs); }
 
+// Shared-memory carve-up, as for the one-CTA kernel: the ring takes what the
+// resident queries, barriers, log and (buffer epilogues) histograms and
+// compaction buffers leave, at most kStages stages -- at d_pad = 384 with
+// resident queries 8 stages of 16 KB (register lists) or 6 (buffer lists),
+// with streamed queries 7 of 32 KB (register lists) or 6.
 struct PairLayout {
   int stages;       // offset of the stage ring (after resident queries)
+  int nstages;      // ring depth
   int stage_bytes;
   int bars;
   int log;
@@ -61,11 +64,16 @@ __host__ __device__ constexpr PairLayout pair_layout(bool qres, int ksl, int sub
   PairLayout l{};
   l.stage_bytes = qres ? kXHalf : (kXHalf + kQSlice);
   l.stages = qres ? ksl * kQSlice : 0;
-  l.bars = l.stages + pair_stages(scratch_keys) * l.stage_bytes;
-  // full[6], empty[6], tfull[2], tempty[2], qfull, done; tmem holder, abort
-  l.log = l.bars + 8 * (2 * kStages + 6) + 16;
+  // full[], empty[], tfull[2], tempty[2], qfull, done; tmem holder, abort; log; histograms; buffers
+  const int bar_bytes = 8 * (2 * kStages + 6) + 16;
+  const int hist_bytes = scratch_keys > 0 ? pair_epi_warps(subs) * 256 * 4 : 0;
+  const int tail = bar_bytes + 8 * kLogSlots + hist_bytes + pair_epi_warps(subs) * scratch_keys * 8;
+  const int n = (kSmemBudget - l.stages - tail) / l.stage_bytes;
+  l.nstages = n < kStages ? n : kStages;
+  l.bars = l.stages + l.nstages * l.stage_bytes;
+  l.log = l.bars + bar_bytes;
   l.hist = l.log + 8 * kLogSlots;
-  l.scratch = l.hist + pair_epi_warps(subs) * 256 * 4;
+  l.scratch = l.hist + hist_bytes;
   l.total = l.scratch + pair_epi_warps(subs) * scratch_keys * 8;
   return l;
 }
@@ -101,12 +109,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
     tc_pair_kernel(const __grid_constant__ CUtensorMap qmap,
                    const __grid_constant__ CUtensorMap xmap, const TcArgs a) {
   constexpr int kEpiWarps = pair_epi_warps(Epi::kSubs);
-  constexpr int kS = pair_stages(Epi::kScratchKeys);  // ring depth
   extern __shared__ uint8_t smem_raw[];
   PairShared sh;
   sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
   sh.l = pair_layout(QRES, a.ksl, Epi::kSubs, Epi::kScratchKeys);
+  const int kS = sh.l.nstages;  // ring depth
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -446,7 +454,7 @@ int pair_clusters_epi(int epi, int ksl) {
 bool tc_pair_resident_queries(int epi, int ksl) {
   const int subs = is_buf_epi(epi) ? EpiTopkBuf<4>::kSubs : 2;
   const int scratch = is_buf_epi(epi) ? EpiTopkBuf<4>::kScratchKeys : 0;
-  return static_cast<size_t>(pair_layout(true, ksl, subs, scratch).total) + 1024 <= 232448;
+  return pair_layout(true, ksl, subs, scratch).nstages >= 6;
 }
 
 int tc_pair_max_clusters(int epi, bool resident_queries, int ksl) {

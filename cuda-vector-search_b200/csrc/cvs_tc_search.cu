@@ -38,21 +38,19 @@ constexpr uint32_t kTmemCols = 512;
 __host__ __device__ constexpr int epi_warps(int subs) { return 4 * subs; }
 __host__ __device__ constexpr int tc_threads(int subs) { return 64 + 32 * epi_warps(subs); }
 
-// Resident queries leave room for 3 corpus stages (96 KB in flight, enough to
-// cover HBM latency); streamed queries use 4 stages of 48 KB, or 3 when the
-// epilogue needs shared-memory compaction buffers.
-__host__ __device__ constexpr int num_stages(bool qres, int scratch_keys) {
-  return (qres || scratch_keys > 0) ? 3 : 4;
-}
-
-// Shared-memory carve-up (offsets from a 1024-byte aligned base).
+// Shared-memory carve-up (offsets from a 1024-byte aligned base): resident
+// query slices (if any), the ring of stages, barriers, iteration log, and for
+// buffer epilogues the per-warp radix histograms and compaction buffers. The
+// ring takes what is left (at most kTcMaxStages stages): resident queries at
+// d_pad = 384 leave 4 stages of 32 KB, streamed queries 4 of 48 KB.
 struct Layout {
   int q_res;      // resident query slices
   int stages;     // ring of stages
+  int nstages;    // ring depth
   int stage_bytes;
   int bars;       // mbarriers
   int log;        // iteration log (cvs_sched.cuh)
-  int hist;       // per epilogue warp radix histograms
+  int hist;       // per epilogue warp radix histograms (buffer epilogue)
   int scratch;    // per epilogue warp compaction buffers (buffer epilogue)
   int total;
 };
@@ -62,11 +60,16 @@ __host__ __device__ constexpr Layout make_layout(bool qres, int ksl, int subs, i
   l.q_res = 0;
   l.stage_bytes = qres ? kXSliceBytes : (kXSliceBytes + kQSliceBytes);
   l.stages = qres ? ksl * kQSliceBytes : 0;
-  l.bars = l.stages + num_stages(qres, scratch_keys) * l.stage_bytes;
-  // full[4], empty[4], tfull[2], tempty[2], qfull, done, tmem holder, abort
-  l.log = l.bars + 8 * (2 * kTcStages + 6) + 16;
+  // full[], empty[], tfull[2], tempty[2], qfull, done, tmem holder, abort; log; histograms; buffers
+  const int bar_bytes = 8 * (2 * kTcMaxStages + 6) + 16;
+  const int hist_bytes = scratch_keys > 0 ? epi_warps(subs) * 256 * 4 : 0;
+  const int tail = bar_bytes + 8 * kLogSlots + hist_bytes + epi_warps(subs) * scratch_keys * 8;
+  const int n = (kSmemBudget - l.stages - tail) / l.stage_bytes;
+  l.nstages = n < kTcMaxStages ? n : kTcMaxStages;
+  l.bars = l.stages + l.nstages * l.stage_bytes;
+  l.log = l.bars + bar_bytes;
   l.hist = l.log + 8 * kLogSlots;
-  l.scratch = l.hist + epi_warps(subs) * 256 * 4;
+  l.scratch = l.hist + hist_bytes;
   l.total = l.scratch + epi_warps(subs) * scratch_keys * 8;
   return l;
 }
@@ -81,16 +84,16 @@ struct Shared {
   }
   __device__ uint64_t* bar(int i) const { return reinterpret_cast<uint64_t*>(base + l.bars) + i; }
   __device__ uint64_t* full(int s) const { return bar(s); }
-  __device__ uint64_t* empty(int s) const { return bar(kTcStages + s); }
-  __device__ uint64_t* tfull(int a) const { return bar(2 * kTcStages + a); }
-  __device__ uint64_t* tempty(int a) const { return bar(2 * kTcStages + 2 + a); }
-  __device__ uint64_t* qfull() const { return bar(2 * kTcStages + 4); }
-  __device__ uint64_t* done() const { return bar(2 * kTcStages + 5); }
+  __device__ uint64_t* empty(int s) const { return bar(kTcMaxStages + s); }
+  __device__ uint64_t* tfull(int a) const { return bar(2 * kTcMaxStages + a); }
+  __device__ uint64_t* tempty(int a) const { return bar(2 * kTcMaxStages + 2 + a); }
+  __device__ uint64_t* qfull() const { return bar(2 * kTcMaxStages + 4); }
+  __device__ uint64_t* done() const { return bar(2 * kTcMaxStages + 5); }
   __device__ uint32_t* tmem_holder() const {
-    return reinterpret_cast<uint32_t*>(base + l.bars + 8 * (2 * kTcStages + 6));
+    return reinterpret_cast<uint32_t*>(base + l.bars + 8 * (2 * kTcMaxStages + 6));
   }
   __device__ volatile int* abort_flag() const {
-    return reinterpret_cast<volatile int*>(base + l.bars + 8 * (2 * kTcStages + 6) + 4);
+    return reinterpret_cast<volatile int*>(base + l.bars + 8 * (2 * kTcMaxStages + 6) + 4);
   }
   __device__ uint64_t* log() const { return reinterpret_cast<uint64_t*>(base + l.log); }
   __device__ uint32_t* hist(int w) const {
@@ -108,12 +111,12 @@ template <bool QRES, class Epi>
 __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     tc_search_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap xmap, const TcArgs a) {
-  constexpr int kS = num_stages(QRES, Epi::kScratchKeys);  // ring depth (barrier arrays are sized for the max)
   extern __shared__ uint8_t smem_raw[];
   Shared sh;
   sh.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
   sh.l = make_layout(QRES, a.ksl, Epi::kSubs, Epi::kScratchKeys);
+  const int kS = sh.l.nstages;  // ring depth
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -386,7 +389,7 @@ bool tc_resident_queries(int epi, int ksl) {
   if (ksl > kTcMaxResidentSlices) return false;
   const int subs = is_buf_epi(epi) ? EpiTopkBuf<4>::kSubs : 2;
   const int scratch = is_buf_epi(epi) ? EpiTopkBuf<4>::kScratchKeys : 0;
-  return static_cast<size_t>(make_layout(true, ksl, subs, scratch).total) + 1024 <= 232448;
+  return make_layout(true, ksl, subs, scratch).nstages >= 3;
 }
 
 int tc_lists_per_segment(int epi) {
