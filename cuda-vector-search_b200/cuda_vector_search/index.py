@@ -103,6 +103,7 @@ class _UploadRing:
 
 
 _RINGS: dict = {}  # device index -> _UploadRing
+_RINGS_LOCK = threading.Lock()
 
 
 def _nothing() -> None:
@@ -113,7 +114,10 @@ def _upload_ring(device: torch.device) -> _UploadRing:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ring = _RINGS.get(idx)
     if ring is None:
-        ring = _RINGS[idx] = _UploadRing(torch.device("cuda", idx))
+        with _RINGS_LOCK:
+            ring = _RINGS.get(idx)
+            if ring is None:
+                ring = _RINGS[idx] = _UploadRing(torch.device("cuda", idx))
     return ring
 
 

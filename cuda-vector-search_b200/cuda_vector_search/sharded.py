@@ -19,6 +19,7 @@ rows and the merge compares (score, global id) keys.
 from __future__ import annotations
 
 import json
+from collections import OrderedDict
 from dataclasses import dataclass
 from pathlib import Path
 from typing import Callable
@@ -62,6 +63,24 @@ class ShardOps:
     local_topk_into: Callable | None = None
 
 
+_CACHED_SHAPES = 4  # (batch, k) shapes whose buffers are kept for reuse
+
+
+def _cached(cache: OrderedDict, key, make):
+    """cache[key], created by make() on a miss; only the most recently used
+    _CACHED_SHAPES entries are kept (a server with varying batch sizes must not
+    accumulate workspaces). A dropped buffer is freed through the caching
+    allocator in stream order, as any tensor."""
+    val = cache.get(key)
+    if val is None:
+        val = cache[key] = make()
+        while len(cache) > _CACHED_SHAPES:
+            cache.popitem(last=False)
+    else:
+        cache.move_to_end(key)
+    return val
+
+
 def _block_bytes(b: int, k: int) -> int:
     """One rank's gathered block: b*k int64 ids, then b*k float32 scores, 8-aligned."""
     return (12 * b * k + 7) // 8 * 8
@@ -80,20 +99,17 @@ def cuda_shard_ops(index: Index) -> ShardOps:
     """Operations backed by this package's kernels for one rank's Index.
 
     The search workspace is allocated once per (batch, k) and reused by later
-    searches of that shape, in stream order on the current stream.
+    searches of that shape, in stream order on the current stream (the last
+    few shapes are kept).
     """
     mod = _ext.load()
-    workspaces: dict = {}
-
+    workspaces: OrderedDict = OrderedDict()
     cosine = index.metric == "cosine"
 
     def workspace(b, kk):
-        ws = workspaces.get((b, kk))
-        if ws is None:
-            ws = torch.empty(max(256, mod.search_workspace_size(b, len(index), index._x.shape[1], kk)),
-                             dtype=torch.uint8, device=index.device)
-            workspaces[(b, kk)] = ws
-        return ws
+        return _cached(workspaces, (b, kk), lambda: torch.empty(
+            max(256, mod.search_workspace_size(b, len(index), index._x.shape[1], kk)), dtype=torch.uint8,
+            device=index.device))
 
     def local_topk_into(queries, k, id_offset, v, i):
         q, release = index._device_queries(queries)
@@ -188,7 +204,7 @@ class ShardedIndex:
         self.shard_sizes = sizes
         self.row_offset = sum(sizes[: self.rank])
         self.n_total = sum(sizes)
-        self._buffers: dict = {}  # (b, k) -> (local block, gathered blocks), reused in stream order
+        self._buffers: OrderedDict = OrderedDict()  # (b, k) -> (local block, gathered blocks), reused in stream order
         # Optional profiling hook: four CUDA events recorded on the current stream
         # before the local search, after it, after the all-gather and after the merge.
         self.phase_events = None
@@ -211,12 +227,11 @@ class ShardedIndex:
         return self.n_total
 
     def _block_pair(self, b: int, k: int, device):
-        bufs = self._buffers.get((b, k))
-        if bufs is None:
+        def make():
             block = torch.empty(_block_bytes(b, k), dtype=torch.uint8, device=device)
-            gathered = torch.empty((self.world, block.numel()), dtype=torch.uint8, device=device)
-            bufs = self._buffers[(b, k)] = (block, gathered)
-        return bufs
+            return block, torch.empty((self.world, block.numel()), dtype=torch.uint8, device=device)
+
+        return _cached(self._buffers, (b, k), make)
 
     def search(self, queries, k: int = 10):
         k = int(k)

@@ -166,3 +166,18 @@ def test_a_rank_without_rows_fails_on_every_rank():
     for rank in (0, 1):
         assert res[rank][0] == "error"
         assert "at least one row" in res[rank][1]
+
+
+def test_shape_cache_keeps_only_recent_shapes():
+    """The per-(batch, k) buffers of the sharded path are bounded (LRU)."""
+    from collections import OrderedDict
+
+    from cuda_vector_search.sharded import _CACHED_SHAPES, _cached
+
+    cache = OrderedDict()
+    made = []
+    for key in [(1, 10), (2, 10), (1, 10), (3, 10), (4, 10), (5, 10), (1, 10)]:
+        _cached(cache, key, lambda key=key: made.append(key) or key)
+    assert len(cache) == _CACHED_SHAPES
+    assert list(cache)[-1] == (1, 10)
+    assert made.count((1, 10)) == 1 and (2, 10) not in cache
