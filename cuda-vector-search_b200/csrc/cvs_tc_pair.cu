@@ -166,6 +166,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
     // ------------------------------ TMA producer (both CTAs) ----------------
     if (elect_one_lane()) {
       const uint64_t pol_x = l2_policy_evict_first();
+      // Dry tiles are read again at the end: keep them in L2 until then.
+      const uint64_t pol_keep = l2_policy_evict_last();
       const uint64_t pol_q = l2_policy_evict_last();
       // Completion of both CTAs' copies is counted on the even CTA's barriers.
       auto even_bar = [&](uint64_t* bar) { return map_to_rank(smem_u32(bar), 0); };
@@ -195,6 +197,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
           break;
         }
         if (v == kLogEnd) break;
+        const uint64_t pol_t = (v & kLogDry) ? pol_keep : pol_x;
         const int row0 = static_cast<int>(v & kLogTileMask) * kTcN + static_cast<int>(rank) * kRows;
         for (int ks = 0; ks < a.ksl; ++ks, ++it) {
           const int s = it % kS;
@@ -204,7 +207,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
             break;
           }
           if (leader) mbar_arrive_expect_tx(sh.full(s), 2 * tx);
-          load(sh.stage_x(s), &xmap, sh.full(s), ks * kTcK, row0, pol_x);
+          load(sh.stage_x(s), &xmap, sh.full(s), ks * kTcK, row0, pol_t);
           if (!QRES) load(sh.stage_q(s), &qmap, sh.full(s), ks * kTcK, qrow0, pol_q);
         }
       }

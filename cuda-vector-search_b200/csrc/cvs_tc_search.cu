@@ -166,6 +166,8 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
     // loaded, so the other roles' waits run out.)
     if (elect_one_lane() && !a.stall) {
       const uint64_t pol_x = l2_policy_evict_first();
+      // Dry tiles are read again at the end: keep them in L2 until then.
+      const uint64_t pol_keep = l2_policy_evict_last();
       const uint64_t pol_q = l2_policy_evict_last();
       const int qrow0 = qt * kTcM;
       if (QRES) {
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
         const uint32_t v = src.next();
         log_put(sh.log(), t, v);
         if (v == kLogEnd) break;
+        const uint64_t pol_t = (v & kLogDry) ? pol_keep : pol_x;
         const int row0 = static_cast<int>(v & kLogTileMask) * kTcN;
         for (int ks = 0; ks < a.ksl; ++ks, ++it) {
           const int s = it % kS;
@@ -191,7 +194,7 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
             break;
           }
           mbar_arrive_expect_tx(sh.full(s), tx);
-          tma_load_2d(sh.stage_x(s), &xmap, sh.full(s), ks * kTcK, row0, pol_x);
+          tma_load_2d(sh.stage_x(s), &xmap, sh.full(s), ks * kTcK, row0, pol_t);
           if (!QRES) tma_load_2d(sh.stage_q(s), &qmap, sh.full(s), ks * kTcK, qrow0, pol_q);
         }
       }
