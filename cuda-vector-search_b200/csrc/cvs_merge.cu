@@ -160,9 +160,15 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
     uint32_t bound = 0;
     if (a.bounds != nullptr) {
       asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(bound) : "l"(a.bounds + q));
-      if (a.tops != nullptr && a.tops_n <= 32 * kMergeTopsPerLane)
-        bound = max(bound, warp_kth_top<kMergeTopsPerLane>(a.tops + static_cast<size_t>(q) * a.tops_n,
-                                                           a.tops_n, a.tops_m, lane));
+      // Per-lane register arrays sized to the list count: the bisection
+      // visits every slot of the array at each of its steps.
+      const uint32_t* tq = a.tops + static_cast<size_t>(q) * a.tops_n;
+      if (a.tops != nullptr) {
+        if (a.tops_n <= 32 * 5) bound = max(bound, warp_kth_top<5>(tq, a.tops_n, a.tops_m, lane));
+        else if (a.tops_n <= 32 * 10) bound = max(bound, warp_kth_top<10>(tq, a.tops_n, a.tops_m, lane));
+        else if (a.tops_n <= 32 * kMergeTopsPerLane)
+          bound = max(bound, warp_kth_top<kMergeTopsPerLane>(tq, a.tops_n, a.tops_m, lane));
+      }
     }
     if (lane == 0) {
       *s_bound = bound;
@@ -291,6 +297,25 @@ __global__ void __launch_bounds__(kKeysThreads) merge_keys_kernel(const MergeKey
       if (lane < cnt && rank < a.k) emit_key(key, rank, a.id_offset, out_v, out_i);
       for (int j = cnt + lane; j < a.k; j += 32) emit_key(0ull, j, a.id_offset, out_v, out_i);
     }
+    return;
+  }
+  if (cnt <= kKeysThreads) {
+    // At most one survivor per thread: each ranks its own against all the
+    // others (shared-memory broadcast reads) and, if it ranks within k, writes
+    // it to its output slot -- one pass of the whole CTA instead of a
+    // single-warp radix select, a gather and a second ranking pass (C4 k=100:
+    // 6.0 -> 3.6 us). Keys are unique, so the ranks are too. (Four survivors
+    // per thread, to cover k = 256, measured slower everywhere: the extra
+    // registers cost the whole kernel.)
+    const int i = threadIdx.x;
+    if (i < cnt) {
+      const uint64_t key = surv[i];
+      int rank = 0;
+#pragma unroll 4
+      for (int t = 0; t < cnt; ++t) rank += surv[t] > key ? 1 : 0;
+      if (rank < a.k) emit_key(key, rank, a.id_offset, out_v, out_i);
+    }
+    for (int j = cnt + i; j < a.k; j += kKeysThreads) emit_key(0ull, j, a.id_offset, out_v, out_i);
     return;
   }
   // k-th best survivor (warp 0), then the winners (keys are unique, so exactly
