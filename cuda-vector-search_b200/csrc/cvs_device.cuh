@@ -64,6 +64,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the waiting thread is parked until the
+// phase completes or about `ns` nanoseconds pass, instead of re-issuing the
+// polling loop (the single-thread producer and MMA loops otherwise spend issue
+// slots, shared with the drain warps of their sub-partition, on spinning).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendNs = 1000000;  // per try_wait; the overall wait stays bounded by kWaitCycles
+
 // Waits for the phase with the given parity to complete. Returns false (after
 // recording kErrTimeout|site in *err and raising *abort) if it does not complete
 // within kWaitCycles, or if another role already raised *abort.
@@ -73,7 +91,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
     if (*abort) return false;
     if (clock64() - t0 > limit) {
       *abort = 1;
@@ -87,7 +105,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // already issued before leaving on an error path.
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_suspend(bar, parity, kSuspendNs)) {
     if (clock64() - t0 > kWaitCycles) return;
   }
 }
