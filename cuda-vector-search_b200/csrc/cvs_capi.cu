@@ -193,6 +193,28 @@ void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks, int epi, i
   p->segs = (p->ntiles + p->tiles_per_seg - 1) / p->tiles_per_seg;
 }
 
+// The GEMV's arithmetic per corpus row grows with the batch, the tcgen05
+// kernel's does not, so from two queries on the tcgen05 kernel streams a large
+// corpus faster. Not a small one: with one tile per CTA there is no dry tile,
+// no query gets a shared bound before its lists fill, and the drain of
+// unbounded per-query lists (one TMEM lane quadrant, so one SM sub-partition,
+// for up to 32 queries) sets the time: 50-65 us at k <= 16, 130-165 us at
+// k <= 32, where the GEMV takes 15-55 us for 2..8 queries. With two tiles per
+// CTA (one dry tile) the bound arrives in time only when the tiles are long to
+// load (d_pad > 512: 30-40 us, faster than the GEMV from four queries on); with
+// shared-memory-resident query tiles (d_pad <= 512) the first real tile is
+// often drained before the other CTAs have published, and the GEMV is as fast
+// at 8 queries and up to 4x faster below. The choice follows the automatic grid
+// (one CTA per SM) even when a segment count is given, so that for a given
+// batch the workspace grows with the segment count along one path.
+bool gemv_preferred(int64_t b, int64_t n, int d_pad, int sms) {
+  if (b <= 1) return true;
+  const int64_t ntiles = (n + kTcN - 1) / kTcN;
+  if (ntiles <= sms) return true;
+  if (ntiles <= static_cast<int64_t>(kDryTiles) * sms) return b <= 2 || d_pad <= 512;
+  return false;
+}
+
 // own_queries: the search ingests its queries itself (cvs_search), into a
 // buffer of whole query tiles at the end of the workspace.
 cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const DeviceInfo& dev,
@@ -201,10 +223,11 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
     return fail(CVS_ERR_INVALID_ARGUMENT, "fused top-k supports 1 <= k <= %d (got %d)", CVS_MAX_FUSED_K, k);
   if (k > n) return fail(CVS_ERR_INVALID_ARGUMENT, "k (%d) must not exceed the corpus size (%lld)", k, (long long)n);
   if (chunks < 0) return fail(CVS_ERR_INVALID_ARGUMENT, "chunks must be >= 0");
-  // bq = 0 (automatic): the CUDA-core GEMV for batches of at most
-  // kGemvMaxBatch queries (beyond that the tcgen05 kernel streams the corpus
-  // faster); an explicit bq asks for the tcgen05 tiles whatever the batch.
-  if (bq == 0 && gemv_supported(static_cast<int>(b), k, d_pad)) {
+  // bq = 0 (automatic): the CUDA-core GEMV for one query, and for up to
+  // kGemvMaxBatch queries on corpora too small for the tcgen05 kernel's dry
+  // tiles (gemv_preferred); an explicit bq asks for the tcgen05 tiles whatever
+  // the batch.
+  if (bq == 0 && gemv_supported(static_cast<int>(b), k, d_pad) && gemv_preferred(b, n, d_pad, dev.sms)) {
     p->gemv = true;
     int segs = chunks > 0 ? chunks : dev.sms * gemv_blocks_per_sm(static_cast<int>(b), d_pad);
     segs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(segs, n)));
@@ -280,7 +303,7 @@ cvs_status launch_search(const Plan& p, const DeviceInfo& dev, const void* q_til
   const int64_t stall_cycles = g_stall_cycles;
   g_stall_cycles = 0;  // one call only
   if (stall_cycles > 0 && (p.gemv || p.pair))
-    return fail(CVS_ERR_INVALID_ARGUMENT, "the stall test hook needs a one-CTA tcgen05 plan (2..128 queries)");
+    return fail(CVS_ERR_INVALID_ARGUMENT, "the stall test hook needs a one-CTA tcgen05 plan (up to 128 queries, not a GEMV plan)");
   uint32_t* bounds = static_cast<uint32_t*>(workspace);
   uint64_t* part = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + p.bound_bytes);
   const bool prof = g_prof_start && g_prof_stop;

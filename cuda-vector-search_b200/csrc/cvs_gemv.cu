@@ -1,9 +1,12 @@
-// CUDA-core GEMV + top-k for a single query (k <= 32): the HBM-bound case.
-// From two queries on, the tcgen05 kernel (with padded query tiles) streams the
-// corpus at least as fast, and from three on this kernel's per-row arithmetic
-// exceeds the stream. Replaces the reference's fused kernel at bq=16 for tiny batches
-// (cuda_vector_search/csrc/kernels.cu:313-371 run with nq = 1, where 15 of
-// its 16 query rows are padding).
+// CUDA-core GEMV + top-k for one to eight queries (k <= 32). One query: the
+// HBM-bound case, at every corpus size. Two to eight: only on corpora too small
+// for the tcgen05 kernel's dry tiles (at most two tiles per CTA), where that
+// kernel's epilogue, not the stream, sets its time; on larger corpora the
+// tcgen05 kernel streams at least as fast from two queries on, and from three
+// on this kernel's per-row arithmetic exceeds the stream. Replaces the
+// reference's fused kernel at bq=16 for tiny batches
+// (cuda_vector_search/csrc/kernels.cu:313-371 run with nq = 1..8, where the
+// other query rows of its 16 are padding).
 //
 // Each warp owns whole corpus rows: lane l reads 16-byte chunks l, l+32, ... of
 // a row (a warp load is 512 contiguous bytes), R rows are loaded before any math
@@ -202,9 +205,15 @@ GemvKernel kernel_nq(int d_pad) {
   }
 }
 
-// The instantiation for one query of width d_pad; CPL = 16-byte chunks per lane
-// per row.
-GemvKernel select_kernel(int, int d_pad) { return kernel_nq<1>(d_pad); }
+// The instantiation for b queries (NQ = 1, 2, 4 or 8: a batch runs in the
+// smallest that holds it, its missing queries zero) of width d_pad; CPL =
+// 16-byte chunks per lane per row.
+GemvKernel select_kernel(int b, int d_pad) {
+  if (b <= 1) return kernel_nq<1>(d_pad);
+  if (b == 2) return kernel_nq<2>(d_pad);
+  if (b <= 4) return kernel_nq<4>(d_pad);
+  return kernel_nq<8>(d_pad);
+}
 
 }  // namespace
 

@@ -105,7 +105,7 @@ cudaError_t tc_pair_launch(int epi, bool resident_queries, const CUtensorMap* qm
 // ---- CUDA-core GEMV + top-k for a single query ------------------------------
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxK = 32;
-constexpr int kGemvMaxBatch = 1;  // queries per GEMV launch (the tcgen05 kernel is as fast beyond)
+constexpr int kGemvMaxBatch = 8;  // queries per GEMV launch (small corpora only from 2 on)
 
 struct GemvArgs {
   const __half* x;    // [n][d_pad]

@@ -68,7 +68,7 @@ def _poll(lib):
 def test_a_wait_that_runs_out_is_reported_and_the_gpu_stays_usable(d):
     lib = _lib()
     assert _poll(lib) == (0, 0), "an earlier kernel left an error behind"
-    x, q = make(4000, d, 8, seed=d)
+    x, q = make(4000, d, 16, seed=d)  # past the GEMV's batches: the one-CTA tcgen05 kernel
     x, q = x.cuda(), q.cuda()
     assert lib.cvs_debug_stall_next_search(1_000_000) == 0
     st, _, _ = _search(lib, q, x, 10)

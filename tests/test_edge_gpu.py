@@ -149,11 +149,17 @@ def test_dry_tile_regimes(cvs, chunks, b, k):
     _check(cvs, x, q, k, chunks=chunks if chunks else None)
 
 
-@pytest.mark.parametrize("b,expect_gemv", [(1, True), (2, False), (3, False), (8, False)])
-def test_plan_selects_gemv_only_for_one_query(cvs, b, expect_gemv):
+# The GEMV takes one query at every corpus size and two to eight queries on
+# corpora too small for the tcgen05 kernel's dry tiles: 5000 rows is 20 tiles
+# (one per CTA), 60000 rows 235 tiles (two per CTA on 148 SMs; d = 256 keeps the
+# query tiles resident), 120000 rows 469 tiles (four per CTA).
+@pytest.mark.parametrize("n,b,expect_gemv", [(5000, 1, True), (5000, 2, True), (5000, 3, True), (5000, 4, True),
+                                             (5000, 5, True), (5000, 8, True), (5000, 9, False), (60000, 8, True),
+                                             (120000, 1, True), (120000, 2, False), (120000, 8, False)])
+def test_plan_selects_gemv(cvs, n, b, expect_gemv):
     from cuda_vector_search import _ext
 
-    x, q = _data(5000, 256, b, seed=b)
+    x, q = _data(n, 256, b, seed=b)
     index = cvs.Index(x.cuda(), metric="ip")
     v, i, plan = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, 10)
     assert (plan.tolist()[0] == b) == expect_gemv  # GEMV plans echo b, tcgen05 plans the tile
