@@ -324,6 +324,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
       if constexpr (is_buf<Epi>::value) epi.redo = (v & kLogRedo) != 0;
       for (int c = sub * kChunks; c < (sub + 1) * kChunks; ++c) {
         if (c * 32 >= valid) break;
+        // A query still without a shared bound (one tile per CTA, or a first
+        // real tile drained before the dry tiles' bound landed) drains every
+        // column of its chunks through the insertion path: it looks for a
+        // bound before each chunk and shares its own k-th best after each.
+        bool unbounded = false;
+        float fb = -INFINITY;
+        if constexpr (!is_store<Epi>::value) {
+          unbounded = !dry && qvalid && epi.bound == -INFINITY;
+          if (unbounded) fb = load_bound(a.gthr + q);
+        }
         uint32_t r[32];
         tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(acc * kTcN + c * 32), r);
         tmem_wait_ld();
@@ -333,12 +343,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(Epi::kS
         } else if (dry) {
           epi.dry(r, nv, qvalid);
         } else {
+          epi.bound = fmaxf(epi.bound, fb);
           epi.consume(r, row0 + c * 32, nv, qvalid, sh.hist(ew));
           if constexpr (is_buf<Epi>::value) {
             epi.compact_lanes(__ballot_sync(kFullMask, qvalid && epi.cnt > a.cap - 32), a,
                               Epi::jrank(a.k, a.segs * Epi::kSubs), sh.hist(ew),
                               sh.scratch(ew, Epi::kScratchKeys), lane);
           }
+          if (unbounded) publish_bound(a.gthr + q, epi.thr, epi.published);
         }
       }
       tc_fence_before();
