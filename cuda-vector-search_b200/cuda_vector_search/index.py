@@ -10,7 +10,7 @@ underneath:
 * search: ``method="fused"`` (the default) is three launches: the queries'
   preparation (to fp16, normalised for cosine, padded) fused with the
   workspace clear, the tcgen05 score + top-k kernel (or the GEMV kernel for a
-  single query), and a merge kernel; queries in pinned host memory are copied
+  single query, and for up to 8 queries on a small corpus), and a merge kernel; queries in pinned host memory are copied
   on a side stream, so a caller that issues the next search before reading
   back the previous results overlaps each upload with the previous search (a
   fixed ring of device buffers, nothing allocated per call);
@@ -258,7 +258,8 @@ class Index:
         """Return (scores [b, k] float32, ids [b, k] int64), best first.
 
         method:
-            "fused"   - tcgen05 (or GEMV for b = 1) scores + top-k in one pass (k <= 1024)
+            "fused"   - tcgen05 (or GEMV for b = 1, and b <= 8 on small corpora) scores + top-k
+                        in one pass (k <= 1024)
             "twopass" - score kernel writes the full matrix, then torch.topk
             "torch"   - torch.matmul (cuBLAS) + torch.topk
             "auto"    - fused when k <= 1024, else twopass

@@ -74,8 +74,9 @@ cvs_status cvs_fused_topk_workspace_size(int64_t b, int64_t n, int d_pad, int k,
  *   out_scores[b][k] (fp32), out_ids[b][k] (int64): best first (score
  *   descending, then smaller id); ids are row indices of x plus id_offset.
  *   workspace: at least cvs_fused_topk_workspace_size() bytes, 256-byte aligned.
- *   plan_bq: query-tile hint, echoed in plan_out[0]: 0 = auto (CUDA-core GEMV
- *   for b = 1 and k <= 32, tcgen05 tiles otherwise), 16..128 = tcgen05, one
+ *   plan_bq: query-tile hint, echoed in plan_out[0]: 0 = auto (CUDA-core GEMV,
+ *   echoing b, for k <= 32 and d_pad <= 1024 when b = 1, or b <= 8 on a corpus
+ *   of at most two 256-row tiles per SM; tcgen05 tiles otherwise), 16..128 = tcgen05, one
  *   CTA per 128-query tile, 256 = CTA pairs (256-query tiles) when b > 128;
  *   plan_chunks: corpus segments per query tile (0 = auto, one CTA per SM).
  *   plan_out (host, may be NULL): {bq, segments actually used}.
