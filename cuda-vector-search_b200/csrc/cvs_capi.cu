@@ -195,24 +195,25 @@ void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks, int epi, i
 
 // The GEMV's arithmetic per corpus row grows with the batch, the tcgen05
 // kernel's does not, so from two queries on the tcgen05 kernel streams a large
-// corpus faster. Not a small one: with one tile per CTA there is no dry tile,
-// no query gets a shared bound before its lists fill, and the drain of
-// unbounded per-query lists (one TMEM lane quadrant, so one SM sub-partition,
-// for up to 32 queries) sets the time: 50-65 us at k <= 16, 130-165 us at
-// k <= 32, where the GEMV takes 15-55 us for 2..8 queries. With two tiles per
-// CTA (one dry tile) the bound arrives in time only when the tiles are long to
-// load (d_pad > 512: 30-40 us, faster than the GEMV from four queries on); with
-// shared-memory-resident query tiles (d_pad <= 512) the first real tile is
-// often drained before the other CTAs have published, and the GEMV is as fast
-// at 8 queries and up to 4x faster below. The choice follows the automatic grid
-// (one CTA per SM) even when a segment count is given, so that for a given
-// batch the workspace grows with the segment count along one path.
-bool gemv_preferred(int64_t b, int64_t n, int d_pad, int sms) {
+// corpus faster. On a small one (at most two tiles per CTA) the tcgen05 kernel
+// costs what its first, dry tile and the wait for a shared bound cost: ~40 us
+// at k <= 16 and ~62 us at k <= 32 with shared-memory-resident query tiles
+// (d_pad <= 640), 20-35 us with longer ones. The GEMV costs ~13 us plus
+// ~0.15 ns per (row x d_pad x query of its instantiation), a little more at
+// k > 16. So for 2..8 queries it is taken on such corpora when d_pad <= 640 and
+// that product stays below 1.5e8 (k <= 16) or 2e8 (k <= 32). Measured: 75000 x
+// 384, b = 4: 0.034 against 0.041 ms, b = 8: 0.066 against 0.045 ms (tcgen05
+// taken); 20000 x 384, b = 8, k = 32: 0.038 against 0.061 ms. The choice follows
+// the automatic grid (one CTA per SM) even when a segment count is given, so
+// that for a given batch the workspace grows with the segment count along one
+// path.
+bool gemv_preferred(int64_t b, int64_t n, int d_pad, int k, int sms) {
   if (b <= 1) return true;
   const int64_t ntiles = (n + kTcN - 1) / kTcN;
-  if (ntiles <= sms) return true;
-  if (ntiles <= static_cast<int64_t>(kDryTiles) * sms) return b <= 2 || d_pad <= 512;
-  return false;
+  if (ntiles > static_cast<int64_t>(kDryTiles) * sms || d_pad > 640) return false;
+  const int64_t nq = b <= 2 ? b : (b <= 4 ? 4 : 8);  // queries the instantiation computes
+  const double work = static_cast<double>(n) * d_pad * nq;
+  return work <= (k <= 16 ? 1.5e8 : 2.0e8);
 }
 
 // own_queries: the search ingests its queries itself (cvs_search), into a
@@ -227,7 +228,7 @@ cvs_status plan_fused(int64_t b, int64_t n, int d_pad, int k, int chunks, const 
   // kGemvMaxBatch queries on corpora too small for the tcgen05 kernel's dry
   // tiles (gemv_preferred); an explicit bq asks for the tcgen05 tiles whatever
   // the batch.
-  if (bq == 0 && gemv_supported(static_cast<int>(b), k, d_pad) && gemv_preferred(b, n, d_pad, dev.sms)) {
+  if (bq == 0 && gemv_supported(static_cast<int>(b), k, d_pad) && gemv_preferred(b, n, d_pad, k, dev.sms)) {
     p->gemv = true;
     int segs = chunks > 0 ? chunks : dev.sms * gemv_blocks_per_sm(static_cast<int>(b), d_pad);
     segs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(segs, n)));

@@ -149,23 +149,40 @@ def test_dry_tile_regimes(cvs, chunks, b, k):
     _check(cvs, x, q, k, chunks=chunks if chunks else None)
 
 
-# The GEMV takes one query at every corpus size and two to eight queries on
-# corpora too small for the tcgen05 kernel's dry tiles: 5000 rows is 20 tiles
-# (one per CTA), 60000 rows 235 tiles (two per CTA on 148 SMs; d = 256 keeps the
-# query tiles resident), 120000 rows 469 tiles (four per CTA).
-@pytest.mark.parametrize("n,b,expect_gemv", [(5000, 1, True), (5000, 2, True), (5000, 3, True), (5000, 4, True),
-                                             (5000, 5, True), (5000, 8, True), (5000, 9, False), (60000, 8, True),
-                                             (120000, 1, True), (120000, 2, False), (120000, 8, False)])
-def test_plan_selects_gemv(cvs, n, b, expect_gemv):
+# The GEMV takes one query at every corpus size, and two to eight queries on
+# corpora of at most two tiles per CTA (5000 rows: 20 tiles; 60000: 235; 148
+# SMs) with resident-width query tiles (d_pad <= 640) while rows x d_pad x the
+# instantiation's queries stays below 1.5e8 (k = 10). 120000 rows is 469 tiles.
+@pytest.mark.parametrize("n,d,b,expect_gemv", [(5000, 256, 1, True), (5000, 256, 2, True), (5000, 256, 3, True),
+                                               (5000, 256, 4, True), (5000, 256, 5, True), (5000, 256, 8, True),
+                                               (5000, 256, 9, False), (60000, 256, 8, True), (60000, 384, 8, False),
+                                               (30000, 1024, 4, False), (120000, 256, 1, True),
+                                               (120000, 256, 2, False), (120000, 256, 8, False)])
+def test_plan_selects_gemv(cvs, n, d, b, expect_gemv):
     from cuda_vector_search import _ext
 
-    x, q = _data(n, 256, b, seed=b)
+    x, q = _data(n, d, b, seed=b)
     index = cvs.Index(x.cuda(), metric="ip")
     v, i, plan = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, 10)
     assert (plan.tolist()[0] == b) == expect_gemv  # GEMV plans echo b, tcgen05 plans the tile
     v2, i2, plan2 = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, 10, 64)
     assert plan2.tolist()[0] == 64  # an explicit bq always selects tcgen05 tiles
     assert torch.equal(i, i2)
+
+
+# The GEMV's 2-, 4- and 8-query instantiations against the oracle (padded
+# query slots of a 3-, 5-, 6- or 7-query batch included), with duplicated rows
+# for exact ties and a ragged width, on plans asserted to be GEMV plans.
+@pytest.mark.parametrize("n,d,b,k,dup", [(3000, 100, 2, 10, 0), (20011, 384, 3, 17, 0), (9000, 640, 4, 32, 1),
+                                         (5000, 256, 5, 10, 2), (12345, 384, 6, 32, 0), (1000, 64, 7, 1, 1),
+                                         (20000, 128, 8, 32, 0), (40, 256, 8, 32, 1)])
+def test_gemv_batches_match_oracle(cvs, n, d, b, k, dup):
+    from cuda_vector_search import _ext
+
+    x, q = _data(n, d, b, seed=n + b, dup=dup)
+    index, v, i = _check(cvs, x, q, k)
+    _, _, plan = _ext.load().fused_topk(index._prep_queries(q.cuda()), index._x, k)
+    assert plan.tolist()[0] == b  # the GEMV plan
 
 
 def test_pinned_host_queries_back_to_back(cvs):
