@@ -139,9 +139,10 @@ def test_no_device_errors_after_edges(cvs):
 
 
 # Dry tiles (each CTA reads its first one or two claimed tiles twice: once to
-# publish bounds, once for real after its last tile) only appear when a CTA gets
-# at least two tiles; chunk overrides and a larger corpus force every regime:
-# 1 tile per CTA (none), 2 (one dry tile), 3 and more (two).
+# publish bounds, once for real after its last tile); chunk overrides and a
+# larger corpus force every regime: 1 tile per CTA (its only tile read dry
+# first), 2 (one dry tile), 3 and more (two). b = 1 and, on the small corpus,
+# b = 3 run on the GEMV instead.
 @pytest.mark.parametrize("chunks", [0, 3, 8, 30, 60])
 @pytest.mark.parametrize("b,k", [(1, 10), (3, 10), (70, 10), (70, 24), (70, 64), (300, 10), (300, 200)])
 def test_dry_tile_regimes(cvs, chunks, b, k):
