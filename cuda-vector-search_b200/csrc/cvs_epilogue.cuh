@@ -46,9 +46,14 @@ __device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
 // k=100 and -4% at C4 k=100, neutral elsewhere.
 __device__ __forceinline__ bool tops_round(int t) { return t < 8 || (t & 15) == 15; }
 
-// The r lists h, h+1, ..., h+r-1 (mod lists) refresh query q in round t.
+// The r lists h, h+1, ..., h+r-1 (mod lists) refresh query q in round t, with
+// h = r * q + a per-round offset: consecutive queries get consecutive windows,
+// so the 32 queries of a drain warp put at most ceil(32 r / lists) + 1 refreshes
+// on any one list (a multiplicative hash put up to 4-5 on some warps, and the
+// slowest warp holds the accumulator for the next MMA): C4 k=100 -0.8%, C2
+// -0.3%.
 __device__ __forceinline__ bool tops_refresher(int q, int t, int list, int lists, int r) {
-  const unsigned h = (static_cast<unsigned>(q) * 2654435761u + static_cast<unsigned>(t) * 40503u) %
+  const unsigned h = (static_cast<unsigned>(q) * static_cast<unsigned>(r) + static_cast<unsigned>(t) * 40503u) %
                      static_cast<unsigned>(lists);
   return (static_cast<unsigned>(list) + static_cast<unsigned>(lists) - h) % static_cast<unsigned>(lists) <
          static_cast<unsigned>(r);
@@ -78,6 +83,27 @@ __device__ __forceinline__ void publish_bound(uint32_t* p, float kth, uint32_t& 
     atomicMax(p, o);
     published = o;
   }
+}
+
+// Plans with a single dry tile (at most two tiles per CTA: small corpora) have
+// their first real tile ready right after the dry one, and a query that drains
+// it before the other CTAs' refreshers have set its bound sends every column of
+// its first chunks through the insertion path. With register lists such queries
+// first poll the bound for up to kBoundPollCycles (~4 us); a timeout is not an
+// error, the drain then runs without one. Measured: 20000 x 384, b = 32
+// 0.041 -> 0.022 ms; 75000 x 384, b = 64, k = 32 0.069 -> 0.033 ms; 20000 x 768,
+// b = 256 (CTA pairs) 0.053 -> 0.035 ms. Not in buffer-list kernels: the code
+// alone (never run there, their large plans have two dry tiles) cost C4 1.6%.
+// Called by the whole warp; p is this lane's query bound, want its query valid.
+constexpr long long kBoundPollCycles = 8000;
+
+static __device__ __noinline__ float poll_bound(const uint32_t* p, bool want, float fresh) {
+  const long long p0 = clock64();
+  while (__any_sync(kFullMask, want && fresh == -INFINITY) && clock64() - p0 < kBoundPollCycles) {
+    __nanosleep(256);
+    if (want && fresh == -INFINITY) fresh = load_bound(p);
+  }
+  return fresh;
 }
 
 // Bit j set when score j is at least lim = max(list threshold, shared bound)

@@ -297,6 +297,12 @@ __global__ void __launch_bounds__(tc_threads(Epi::kSubs), 1)
       tc_fence_after();
       if constexpr (!is_store<Epi>::value) {
         if (qvalid && t == nd && nd > 0) fresh = load_bound(a.gthr + q);
+        if constexpr (Epi::kTops && !is_buf<Epi>::value) {
+          // Single-dry-tile plans (small corpora): see poll_bound.
+          const int lists = a.segs * Epi::kSubs;
+          if (t == nd && nd == 1 && lists <= 32 * kTopsPerLane && lists >= a.k)
+            fresh = poll_bound(a.gthr + q, qvalid, fresh);
+        }
         epi.bound = fmaxf(epi.bound, fresh);
       }
       const int row0 = static_cast<int>(v & kLogTileMask) * kTcN;
