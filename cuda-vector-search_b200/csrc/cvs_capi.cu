@@ -195,25 +195,27 @@ void plan_tc_grid(Plan* p, int64_t b, int64_t n, int sms, int chunks, int epi, i
 
 // The GEMV's arithmetic per corpus row grows with the batch, the tcgen05
 // kernel's does not, so from two queries on the tcgen05 kernel streams a large
-// corpus faster. On a small one (at most two tiles per CTA) the tcgen05 kernel
-// costs what its first, dry tile and the wait for a shared bound cost: ~40 us
-// at k <= 16 and ~62 us at k <= 32 with shared-memory-resident query tiles
-// (d_pad <= 640), 20-35 us with longer ones. The GEMV costs ~13 us plus
-// ~0.15 ns per (row x d_pad x query of its instantiation), a little more at
-// k > 16. So for 2..8 queries it is taken on such corpora when d_pad <= 640 and
-// that product stays below 1.5e8 (k <= 16) or 2e8 (k <= 32). Measured: 75000 x
-// 384, b = 4: 0.034 against 0.041 ms, b = 8: 0.066 against 0.045 ms (tcgen05
-// taken); 20000 x 384, b = 8, k = 32: 0.038 against 0.061 ms. The choice follows
-// the automatic grid (one CTA per SM) even when a segment count is given, so
-// that for a given batch the workspace grows with the segment count along one
-// path.
+// corpus faster. On a small one (at most two tiles per CTA, one dry tile) the
+// tcgen05 kernel costs what its dry tile and the wait for a shared bound cost:
+// 17-25 us at k <= 16 with d_pad <= 640, while at k <= 32 a query whose bound
+// comes late drains 32-slot register lists without one (24-135 us measured,
+// varying from run to run). The GEMV costs ~13 us plus ~0.15 ns per (row x
+// max(d_pad, 256) x query of its instantiation) -- narrow rows do not get
+// cheaper than 256 columns, the shuffle reduction per row and query stays. So
+// for 2..8 queries it is taken on such corpora when d_pad <= 640 and that
+// product stays below 3e7 (k <= 16) or 1.2e8 (k <= 32). Measured, GEMV against
+// tcgen05: 20000 x 384, b = 2: 0.014 / 0.019 ms; b = 8: 0.033 / 0.021 ms
+// (tcgen05 taken); 20000 x 128, b = 8: 0.027 / 0.017 ms (tcgen05 taken); 75000 x
+// 384, b = 4, k = 32: 0.041 / 0.135 ms. The choice follows the automatic grid
+// (one CTA per SM) even when a segment count is given, so that for a given
+// batch the workspace grows with the segment count along one path.
 bool gemv_preferred(int64_t b, int64_t n, int d_pad, int k, int sms) {
   if (b <= 1) return true;
   const int64_t ntiles = (n + kTcN - 1) / kTcN;
   if (ntiles > static_cast<int64_t>(kDryTiles) * sms || d_pad > 640) return false;
   const int64_t nq = b <= 2 ? b : (b <= 4 ? 4 : 8);  // queries the instantiation computes
-  const double work = static_cast<double>(n) * d_pad * nq;
-  return work <= (k <= 16 ? 1.5e8 : 2.0e8);
+  const double work = static_cast<double>(n) * std::max(d_pad, 256) * nq;
+  return work <= (k <= 16 ? 3.0e7 : 1.2e8);
 }
 
 // own_queries: the search ingests its queries itself (cvs_search), into a

@@ -152,11 +152,13 @@ def test_dry_tile_regimes(cvs, chunks, b, k):
 
 # The GEMV takes one query at every corpus size, and two to eight queries on
 # corpora of at most two tiles per CTA (5000 rows: 20 tiles; 60000: 235; 148
-# SMs) with resident-width query tiles (d_pad <= 640) while rows x d_pad x the
-# instantiation's queries stays below 1.5e8 (k = 10). 120000 rows is 469 tiles.
+# SMs) with resident-width query tiles (d_pad <= 640) while rows x
+# max(d_pad, 256) x the instantiation's queries stays below 3e7 (k = 10).
+# 120000 rows is 469 tiles.
 @pytest.mark.parametrize("n,d,b,expect_gemv", [(5000, 256, 1, True), (5000, 256, 2, True), (5000, 256, 3, True),
                                                (5000, 256, 4, True), (5000, 256, 5, True), (5000, 256, 8, True),
-                                               (5000, 256, 9, False), (60000, 256, 8, True), (60000, 384, 8, False),
+                                               (5000, 256, 9, False), (12000, 256, 8, True), (12000, 128, 8, True),
+                                               (60000, 256, 2, False), (60000, 256, 8, False),
                                                (30000, 1024, 4, False), (120000, 256, 1, True),
                                                (120000, 256, 2, False), (120000, 256, 8, False)])
 def test_plan_selects_gemv(cvs, n, d, b, expect_gemv):
