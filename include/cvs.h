@@ -75,8 +75,10 @@ cvs_status cvs_fused_topk_workspace_size(int64_t b, int64_t n, int d_pad, int k,
  *   descending, then smaller id); ids are row indices of x plus id_offset.
  *   workspace: at least cvs_fused_topk_workspace_size() bytes, 256-byte aligned.
  *   plan_bq: query-tile hint, echoed in plan_out[0]: 0 = auto (CUDA-core GEMV,
- *   echoing b, for k <= 32 and d_pad <= 1024 when b = 1, or b <= 8 on a corpus
- *   of at most two 256-row tiles per SM; tcgen05 tiles otherwise), 16..128 = tcgen05, one
+ *   echoing b, for k <= 32 and d_pad <= 1024 when b = 1, or for b <= 8 on a
+ *   small corpus: at most two 256-row tiles per SM, d_pad <= 640 and
+ *   n x max(d_pad, 256) x (2, 4 or 8) <= 3e7 at k <= 16, 1.2e8 at k <= 32;
+ *   tcgen05 tiles otherwise), 16..128 = tcgen05, one
  *   CTA per 128-query tile, 256 = CTA pairs (256-query tiles) when b > 128;
  *   plan_chunks: corpus segments per query tile (0 = auto, one CTA per SM).
  *   plan_out (host, may be NULL): {bq, segments actually used}.
