@@ -425,15 +425,15 @@ struct EpiTopkBuf {
   static __device__ __forceinline__ bool dry_ok(const TcArgs& a) { return tops_j(a.k, a.segs * kSubs, RJ) <= kRegJ; }
   __device__ __forceinline__ void dry(const uint32_t (&r)[32], int nvalid, bool qvalid) {
     if (!qvalid) return;
-    // Only scores that beat the kRegJ-th tracked one can change tj.
+    // Only scores that beat the kRegJ-th tracked one can change tj; when one
+    // does, all 32 go through the compare-exchange chain with static register
+    // indices (2 kRegJ min/max each; a score at or below tj's last entry leaves
+    // it unchanged). Selecting the candidates one by one cost ~60 instructions
+    // each, and a fresh list's first chunk has 32 of them.
     const float lo = tj[kRegJ - 1];
     if (!(max_valid(r, nvalid) > lo)) return;
-    uint32_t m = above_mask(r, lo, nvalid);
-    while (m) {
-      const int j = __ffs(m) - 1;
-      m &= m - 1;
-      track(pick(r, j));
-    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) track(j < nvalid ? __uint_as_float(r[j]) : -INFINITY);
   }
 
   // The list's segment holds at least J rows scoring >= best (the value is the
