@@ -1,9 +1,10 @@
 // CUDA-core GEMV + top-k for one to eight queries (k <= 32). One query: the
-// HBM-bound case, at every corpus size. Two to eight: only on corpora too small
-// for the tcgen05 kernel's dry tiles (at most two tiles per CTA), where that
-// kernel's epilogue, not the stream, sets its time; on larger corpora the
-// tcgen05 kernel streams at least as fast from two queries on, and from three
-// on this kernel's per-row arithmetic exceeds the stream. Replaces the
+// HBM-bound case, at every corpus size. Two to eight: only on small corpora
+// (at most two tiles per CTA for the tcgen05 kernel, and little work: the
+// planner's gemv_preferred), where that kernel's dry tile and bound wait, not
+// the stream, set its time; on larger corpora the tcgen05 kernel streams at
+// least as fast from two queries on, and from three on this kernel's per-row
+// arithmetic exceeds the stream. Replaces the
 // reference's fused kernel at bq=16 for tiny batches
 // (cuda_vector_search/csrc/kernels.cu:313-371 run with nq = 1..8, where the
 // other query rows of its 16 are padding).

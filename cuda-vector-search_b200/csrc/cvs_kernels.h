@@ -102,7 +102,7 @@ int tc_pair_max_clusters(int epi, bool resident_queries, int ksl);
 cudaError_t tc_pair_launch(int epi, bool resident_queries, const CUtensorMap* qmap,
                            const CUtensorMap* xmap, const TcArgs& a, cudaStream_t stream);
 
-// ---- CUDA-core GEMV + top-k for a single query ------------------------------
+// ---- CUDA-core GEMV + top-k for one to eight queries -----------------------
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxK = 32;
 constexpr int kGemvMaxBatch = 8;  // queries per GEMV launch (small corpora only from 2 on)
